@@ -1,0 +1,113 @@
+/*
+ * metellus_b200.h — C ABI of the Metellus B200 backend (libmetellus_cuda.so).
+ *
+ * This library replaces the reference's Objective-C++ nanobind module
+ * `metal_backend` (src/metal_backend.mm:253-261). Every entry point returns an int
+ * status: 0 = success, nonzero = failure, with the message available from
+ * mt_last_error(). The Python layer raises RuntimeError on nonzero, matching the
+ * reference's std::runtime_error -> RuntimeError behaviour (metal_backend.mm:78,
+ * 192-207, 230-232).
+ *
+ * Threading: one CUDA stream per device; the buffer registry and kernel table are
+ * mutex-guarded. Device work is stream ordered; reads synchronise the stream.
+ */
+#ifndef METELLUS_B200_H
+#define METELLUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- errors / devices --------------------------------------------------- */
+
+/* Copy the calling thread's last error message into buf (NUL terminated). */
+int mt_last_error(char* buf, size_t n);
+/* Number of visible CUDA devices. */
+int mt_device_count(int* n);
+/* Initialise device `dev` (primary context, stream, memory pool). Idempotent.
+ * The reference creates its device and queue statically (metal_backend.mm:21-35). */
+int mt_init(int dev);
+/* Query a device attribute: 0 = SM count, 1 = max opt-in shared memory per block,
+ * 2 = compute capability major*10+minor, 3 = L2 bytes. */
+int mt_device_attr(int dev, int which, int64_t* out);
+
+/* ---- buffers (replace create_buffer / release_buffer / buffer_size /
+ *      write_buffer / read_buffer / fill_buffer, metal_backend.mm:94-141) ---- */
+
+/* Allocate nbytes of device memory on `dev` from a stream-ordered pool. */
+int mt_buffer_create(int dev, size_t nbytes, uint64_t* handle);
+/* Release a buffer (stream ordered: pending kernels that use it finish first). */
+int mt_buffer_release(uint64_t handle);
+int mt_buffer_size(uint64_t handle, size_t* nbytes);
+/* Device address of the buffer (for interop and for the C-level tests). */
+int mt_buffer_ptr(uint64_t handle, uint64_t* dptr);
+/* Host -> device copy of nbytes from src (pinned or pageable); waits for completion. */
+int mt_buffer_write(uint64_t handle, const void* src, size_t nbytes);
+/* Device -> host copy into dst; waits for all earlier work on the stream. */
+int mt_buffer_read(uint64_t handle, void* dst, size_t nbytes);
+/* Asynchronous variants (stream ordered); src/dst must be pinned for true overlap. */
+int mt_buffer_write_async(uint64_t handle, const void* src, size_t nbytes);
+int mt_buffer_read_async(uint64_t handle, void* dst, size_t nbytes);
+/* Set every byte to `value`. */
+int mt_buffer_fill(uint64_t handle, uint8_t value);
+/* Pinned host memory for fast host<->device copies. */
+int mt_host_alloc(size_t nbytes, void** ptr);
+int mt_host_free(void* ptr);
+
+/* ---- kernels (replace run_kernel's per-call compile, metal_backend.mm:178-249) */
+
+/* NVRTC: compile CUDA C++ `src` for `arch` (e.g. "sm_100a") with extra options
+ * (space separated) into a cubin. On success *size is the cubin size; if cap is
+ * too small nothing is copied and the call still succeeds (query then retry).
+ * The compile log goes to `log` (may be NULL). */
+int mt_nvrtc_compile(const char* src, const char* name, const char* opts,
+                     void* cubin, size_t cap, size_t* size, char* log, size_t logcap);
+/* Load a cubin and look up `fn`; returns a kernel handle usable on any device. */
+int mt_kernel_load(const void* cubin, size_t size, const char* fn, uint64_t* kernel);
+/* Register count and local (spill) bytes per thread of a loaded kernel. */
+int mt_kernel_info(int dev, uint64_t kernel, int* regs, int* local_bytes, int* max_threads);
+
+/* TMA tensor-map description, encoded by the backend at launch time. */
+typedef struct mt_tmap_spec {
+    int32_t buf_index;     /* index into the launch's buffer list */
+    uint32_t rank;         /* 1..5 */
+    uint64_t dims[5];      /* elements, innermost first */
+    uint64_t strides[4];   /* bytes, for dims 1..rank-1 */
+    uint32_t box[5];       /* elements per copy, innermost first */
+    uint32_t elem_strides[5];
+    int32_t swizzle;       /* 0 none, 1 32B, 2 64B, 3 128B */
+    int32_t l2_promo;      /* 0 none, 1 64B, 2 128B, 3 256B */
+    uint64_t byte_offset;  /* added to the buffer base address */
+} mt_tmap_spec;
+
+/* Launch `kernel` on device `dev`'s stream. Parameters are the buffers' device
+ * addresses in order, then a 64-byte block holding `ndims` uint32 dims, then one
+ * CUtensorMap per tmap spec. If time_ms is non-NULL the launch is bracketed by
+ * events, waited for, and its device time is returned (profile mode). cluster_x
+ * > 1 launches thread-block clusters of that size along x. */
+int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf,
+              const uint32_t* dims, int ndims, const uint32_t grid[3],
+              const uint32_t block[3], uint32_t dyn_smem, uint32_t cluster_x,
+              const mt_tmap_spec* tmaps, int ntmaps, float* time_ms);
+/* Wait for all work on the device's stream. */
+int mt_sync(int dev);
+
+/* ---- timing and graphs --------------------------------------------------- */
+
+int mt_event_create(uint64_t* ev);
+int mt_event_record(int dev, uint64_t ev);
+int mt_event_elapsed(uint64_t start, uint64_t end, float* ms);
+int mt_event_destroy(uint64_t ev);
+/* Capture subsequent launches on the device's stream into a CUDA graph. */
+int mt_graph_begin(int dev);
+int mt_graph_end(int dev, uint64_t* graph);
+int mt_graph_launch(int dev, uint64_t graph);
+int mt_graph_destroy(uint64_t graph);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* METELLUS_B200_H */

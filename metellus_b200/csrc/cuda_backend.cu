@@ -1,0 +1,540 @@
+// Native backend of Metellus for NVIDIA B200 (sm_100a): the C ABI declared in
+// include/metellus_b200.h. It takes over from the reference's Objective-C++ Metal
+// backend (src/metal_backend.mm): where that module recompiles MSL on every
+// run_kernel call and waits for each command buffer, this one compiles once with
+// NVRTC (the Python layer keeps an on-disk cubin cache), allocates from a
+// stream-ordered memory pool, launches asynchronously on one stream per device and
+// only synchronises on reads, explicit syncs and profile-mode launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nvrtc.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/metellus_b200.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+// Driver API entry points, resolved through the runtime at first use so that the
+// library loads (and exports its symbols) on machines without a GPU driver.
+struct DriverApi {
+    decltype(&cuModuleLoadData) ModuleLoadData = nullptr;
+    decltype(&cuModuleGetFunction) ModuleGetFunction = nullptr;
+    decltype(&cuFuncSetAttribute) FuncSetAttribute = nullptr;
+    decltype(&cuFuncGetAttribute) FuncGetAttribute = nullptr;
+    decltype(&cuLaunchKernel) LaunchKernel = nullptr;
+    decltype(&cuLaunchKernelEx) LaunchKernelEx = nullptr;
+    decltype(&cuTensorMapEncodeTiled) TensorMapEncodeTiled = nullptr;
+    decltype(&cuGetErrorString) GetErrorString = nullptr;
+    bool ok = false;
+} g_drv;
+
+int fail(const char* fmt, ...) {
+    char buf[2048];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return 1;
+}
+
+#define RT_CHECK(call)                                                               \
+    do {                                                                             \
+        cudaError_t e_ = (call);                                                     \
+        if (e_ != cudaSuccess)                                                       \
+            return fail("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_),      \
+                        __FILE__, __LINE__);                                         \
+    } while (0)
+
+#define DRV_CHECK(call)                                                              \
+    do {                                                                             \
+        if (load_driver()) return 1;                                                 \
+        CUresult r_ = (g_drv.call);                                                  \
+        if (r_ != CUDA_SUCCESS) {                                                    \
+            const char* s_ = nullptr;                                                \
+            if (g_drv.GetErrorString) g_drv.GetErrorString(r_, &s_);                 \
+            return fail("%s failed: %s (%s:%d)", #call, s_ ? s_ : "?", __FILE__,     \
+                        __LINE__);                                                   \
+        }                                                                            \
+    } while (0)
+
+int load_driver() {
+    if (g_drv.ok) return 0;
+    cudaDriverEntryPointQueryResult q;
+#define MT_SYM(field, name)                                                                   \
+    if (cudaGetDriverEntryPoint(name, (void**)&g_drv.field, cudaEnableDefault, &q) != cudaSuccess || \
+        !g_drv.field)                                                                         \
+        return fail("driver entry point %s unavailable", name);
+    MT_SYM(ModuleLoadData, "cuModuleLoadData")
+    MT_SYM(ModuleGetFunction, "cuModuleGetFunction")
+    MT_SYM(FuncSetAttribute, "cuFuncSetAttribute")
+    MT_SYM(FuncGetAttribute, "cuFuncGetAttribute")
+    MT_SYM(LaunchKernel, "cuLaunchKernel")
+    MT_SYM(LaunchKernelEx, "cuLaunchKernelEx")
+    MT_SYM(TensorMapEncodeTiled, "cuTensorMapEncodeTiled")
+    MT_SYM(GetErrorString, "cuGetErrorString")
+#undef MT_SYM
+    g_drv.ok = true;
+    return 0;
+}
+
+constexpr int kMaxDev = 16;
+
+struct Device {
+    bool ready = false;
+    cudaStream_t stream = nullptr;
+    cudaMemPool_t pool = nullptr;
+};
+
+struct Buffer {
+    int dev;
+    void* ptr;
+    size_t size;
+};
+
+struct KernelEntry {
+    std::vector<char> cubin;
+    std::string fn;
+    CUmodule mod[kMaxDev] = {};
+    CUfunction func[kMaxDev] = {};
+    int smem_attr[kMaxDev] = {};
+};
+
+std::mutex g_mu;
+Device g_dev[kMaxDev];
+std::map<uint64_t, Buffer> g_bufs;
+std::map<uint64_t, std::unique_ptr<KernelEntry>> g_kernels;
+std::map<uint64_t, cudaEvent_t> g_events;
+std::map<uint64_t, cudaGraphExec_t> g_graphs;
+uint64_t g_next = 1;
+
+int ensure_dev(int dev) {
+    if (dev < 0 || dev >= kMaxDev) return fail("device index %d out of range", dev);
+    Device& d = g_dev[dev];
+    RT_CHECK(cudaSetDevice(dev));
+    if (d.ready) return 0;
+    RT_CHECK(cudaFree(nullptr));  // create / bind the primary context
+    RT_CHECK(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+    RT_CHECK(cudaDeviceGetDefaultMemPool(&d.pool, dev));
+    uint64_t keep = ~0ull;  // keep freed blocks cached in the pool
+    RT_CHECK(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    d.ready = true;
+    return 0;
+}
+
+int get_buf(uint64_t h, Buffer* out) {
+    auto it = g_bufs.find(h);
+    if (it == g_bufs.end()) return fail("unknown buffer handle %llu", (unsigned long long)h);
+    *out = it->second;
+    return 0;
+}
+
+int get_func(KernelEntry* k, int dev, CUfunction* f) {
+    if (!k->func[dev]) {
+        DRV_CHECK(ModuleLoadData(&k->mod[dev], k->cubin.data()));
+        DRV_CHECK(ModuleGetFunction(&k->func[dev], k->mod[dev], k->fn.c_str()));
+    }
+    *f = k->func[dev];
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mt_last_error(char* buf, size_t n) {
+    if (!buf || n == 0) return 1;
+    snprintf(buf, n, "%s", g_err.c_str());
+    return 0;
+}
+
+int mt_device_count(int* n) {
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) {
+        *n = 0;
+        cudaGetLastError();
+        return 0;
+    }
+    *n = c;
+    return 0;
+}
+
+int mt_init(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return ensure_dev(dev);
+}
+
+int mt_device_attr(int dev, int which, int64_t* out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    int v = 0;
+    switch (which) {
+        case 0: RT_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev)); break;
+        case 1: RT_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)); break;
+        case 2: {
+            int a = 0, b = 0;
+            RT_CHECK(cudaDeviceGetAttribute(&a, cudaDevAttrComputeCapabilityMajor, dev));
+            RT_CHECK(cudaDeviceGetAttribute(&b, cudaDevAttrComputeCapabilityMinor, dev));
+            v = a * 10 + b;
+            break;
+        }
+        case 3: RT_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrL2CacheSize, dev)); break;
+        default: return fail("unknown attribute %d", which);
+    }
+    *out = v;
+    return 0;
+}
+
+int mt_buffer_create(int dev, size_t nbytes, uint64_t* handle) {
+    if (nbytes == 0) return fail("buffer nbytes must be > 0");
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    void* p = nullptr;
+    RT_CHECK(cudaMallocAsync(&p, nbytes, g_dev[dev].pool, g_dev[dev].stream));
+    uint64_t h = g_next++;
+    g_bufs[h] = Buffer{dev, p, nbytes};
+    *handle = h;
+    return 0;
+}
+
+int mt_buffer_release(uint64_t handle) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Buffer b;
+    if (get_buf(handle, &b)) return 1;
+    RT_CHECK(cudaSetDevice(b.dev));
+    RT_CHECK(cudaFreeAsync(b.ptr, g_dev[b.dev].stream));
+    g_bufs.erase(handle);
+    return 0;
+}
+
+int mt_buffer_size(uint64_t handle, size_t* nbytes) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Buffer b;
+    if (get_buf(handle, &b)) return 1;
+    *nbytes = b.size;
+    return 0;
+}
+
+int mt_buffer_ptr(uint64_t handle, uint64_t* dptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Buffer b;
+    if (get_buf(handle, &b)) return 1;
+    *dptr = (uint64_t)(uintptr_t)b.ptr;
+    return 0;
+}
+
+static int copy_common(uint64_t handle, void* host, size_t nbytes, bool to_dev, bool wait) {
+    Buffer b;
+    cudaStream_t s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (get_buf(handle, &b)) return 1;
+        s = g_dev[b.dev].stream;
+    }
+    if (nbytes > b.size) return fail("copy of %zu bytes exceeds buffer of %zu bytes", nbytes, b.size);
+    RT_CHECK(cudaSetDevice(b.dev));
+    if (to_dev)
+        RT_CHECK(cudaMemcpyAsync(b.ptr, host, nbytes, cudaMemcpyHostToDevice, s));
+    else
+        RT_CHECK(cudaMemcpyAsync(host, b.ptr, nbytes, cudaMemcpyDeviceToHost, s));
+    if (wait) RT_CHECK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int mt_buffer_write(uint64_t h, const void* src, size_t n) { return copy_common(h, (void*)src, n, true, true); }
+int mt_buffer_read(uint64_t h, void* dst, size_t n) { return copy_common(h, dst, n, false, true); }
+int mt_buffer_write_async(uint64_t h, const void* src, size_t n) { return copy_common(h, (void*)src, n, true, false); }
+int mt_buffer_read_async(uint64_t h, void* dst, size_t n) { return copy_common(h, dst, n, false, false); }
+
+int mt_buffer_fill(uint64_t handle, uint8_t value) {
+    Buffer b;
+    cudaStream_t s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (get_buf(handle, &b)) return 1;
+        s = g_dev[b.dev].stream;
+    }
+    RT_CHECK(cudaSetDevice(b.dev));
+    RT_CHECK(cudaMemsetAsync(b.ptr, value, b.size, s));
+    RT_CHECK(cudaStreamSynchronize(s));
+    return 0;
+}
+
+int mt_host_alloc(size_t nbytes, void** ptr) {
+    RT_CHECK(cudaHostAlloc(ptr, nbytes, cudaHostAllocPortable));
+    return 0;
+}
+
+int mt_host_free(void* ptr) {
+    RT_CHECK(cudaFreeHost(ptr));
+    return 0;
+}
+
+int mt_nvrtc_compile(const char* src, const char* name, const char* opts, void* cubin, size_t cap,
+                     size_t* size, char* log, size_t logcap) {
+    nvrtcProgram prog;
+    nvrtcResult r = nvrtcCreateProgram(&prog, src, name ? name : "kernel.cu", 0, nullptr, nullptr);
+    if (r != NVRTC_SUCCESS) return fail("nvrtcCreateProgram: %s", nvrtcGetErrorString(r));
+    std::vector<std::string> args;
+    {
+        std::string o = opts ? opts : "";
+        size_t i = 0;
+        while (i < o.size()) {
+            while (i < o.size() && o[i] == ' ') ++i;
+            size_t j = i;
+            while (j < o.size() && o[j] != ' ') ++j;
+            if (j > i) args.push_back(o.substr(i, j - i));
+            i = j;
+        }
+    }
+    std::vector<const char*> argv;
+    for (auto& a : args) argv.push_back(a.c_str());
+    r = nvrtcCompileProgram(prog, (int)argv.size(), argv.data());
+    size_t lsz = 0;
+    nvrtcGetProgramLogSize(prog, &lsz);
+    std::string lg(lsz, '\0');
+    if (lsz) nvrtcGetProgramLog(prog, &lg[0]);
+    if (log && logcap) snprintf(log, logcap, "%s", lg.c_str());
+    if (r != NVRTC_SUCCESS) {
+        nvrtcDestroyProgram(&prog);
+        return fail("NVRTC compile of %s failed: %s\n%s", name ? name : "kernel", nvrtcGetErrorString(r),
+                    lg.c_str());
+    }
+    size_t n = 0;
+    r = nvrtcGetCUBINSize(prog, &n);
+    if (r != NVRTC_SUCCESS) {
+        nvrtcDestroyProgram(&prog);
+        return fail("nvrtcGetCUBINSize: %s", nvrtcGetErrorString(r));
+    }
+    *size = n;
+    if (cubin && cap >= n) nvrtcGetCUBIN(prog, (char*)cubin);
+    nvrtcDestroyProgram(&prog);
+    return 0;
+}
+
+int mt_kernel_load(const void* cubin, size_t size, const char* fn, uint64_t* kernel) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto k = std::make_unique<KernelEntry>();
+    k->cubin.assign((const char*)cubin, (const char*)cubin + size);
+    k->fn = fn;
+    uint64_t h = g_next++;
+    g_kernels[h] = std::move(k);
+    *kernel = h;
+    return 0;
+}
+
+int mt_kernel_info(int dev, uint64_t kernel, int* regs, int* local_bytes, int* max_threads) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    auto it = g_kernels.find(kernel);
+    if (it == g_kernels.end()) return fail("unknown kernel handle");
+    CUfunction f;
+    if (get_func(it->second.get(), dev, &f)) return 1;
+    DRV_CHECK(FuncGetAttribute(regs, CU_FUNC_ATTRIBUTE_NUM_REGS, f));
+    DRV_CHECK(FuncGetAttribute(local_bytes, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f));
+    DRV_CHECK(FuncGetAttribute(max_threads, CU_FUNC_ATTRIBUTE_MAX_THREADS_PER_BLOCK, f));
+    return 0;
+}
+
+int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf, const uint32_t* dims,
+              int ndims, const uint32_t grid[3], const uint32_t block[3], uint32_t dyn_smem,
+              uint32_t cluster_x, const mt_tmap_spec* tmaps, int ntmaps, float* time_ms) {
+    if (ndims < 0 || ndims > 16) return fail("ndims %d out of range (max 16)", ndims);
+    if (nbuf < 0 || nbuf > 64) return fail("nbuf %d out of range (max 64)", nbuf);
+    if (ntmaps < 0 || ntmaps > 8) return fail("ntmaps %d out of range (max 8)", ntmaps);
+    CUfunction f;
+    cudaStream_t s;
+    std::vector<uint64_t> ptrs(nbuf);
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_dev(dev)) return 1;
+        auto it = g_kernels.find(kernel);
+        if (it == g_kernels.end()) return fail("unknown kernel handle %llu", (unsigned long long)kernel);
+        KernelEntry* k = it->second.get();
+        if (get_func(k, dev, &f)) return 1;
+        if ((int)dyn_smem > k->smem_attr[dev]) {
+            DRV_CHECK(FuncSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)dyn_smem));
+            k->smem_attr[dev] = (int)dyn_smem;
+        }
+        for (int i = 0; i < nbuf; ++i) {
+            Buffer b;
+            if (get_buf(buffers[i], &b)) return 1;
+            if (b.dev != dev) return fail("buffer %d lives on device %d, launch is on %d", i, b.dev, dev);
+            ptrs[i] = (uint64_t)(uintptr_t)b.ptr;
+        }
+        s = g_dev[dev].stream;
+    }
+    struct alignas(64) Dims { uint32_t d[16]; } dimblk;
+    memset(&dimblk, 0, sizeof dimblk);
+    for (int i = 0; i < ndims; ++i) dimblk.d[i] = dims[i];
+    std::vector<CUtensorMap> maps(ntmaps > 0 ? ntmaps : 1);
+    for (int t = 0; t < ntmaps; ++t) {
+        const mt_tmap_spec& sp = tmaps[t];
+        if (sp.buf_index < 0 || sp.buf_index >= nbuf) return fail("tmap %d: bad buffer index", t);
+        static const CUtensorMapSwizzle sw[] = {CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                                                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_SWIZZLE_128B};
+        static const CUtensorMapL2promotion l2[] = {
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B};
+        if (sp.swizzle < 0 || sp.swizzle > 3 || sp.l2_promo < 0 || sp.l2_promo > 3)
+            return fail("tmap %d: bad swizzle / l2 promotion", t);
+        cuuint64_t gdim[5], gstr[4];
+        cuuint32_t box[5], es[5];
+        for (uint32_t i = 0; i < sp.rank; ++i) {
+            gdim[i] = sp.dims[i];
+            box[i] = sp.box[i];
+            es[i] = sp.elem_strides[i] ? sp.elem_strides[i] : 1;
+        }
+        for (uint32_t i = 0; i + 1 < sp.rank; ++i) gstr[i] = sp.strides[i];
+        void* base = (void*)(uintptr_t)(ptrs[sp.buf_index] + sp.byte_offset);
+        DRV_CHECK(TensorMapEncodeTiled(&maps[t], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sp.rank, base, gdim,
+                                         gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw[sp.swizzle],
+                                         l2[sp.l2_promo], CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE));
+    }
+    std::vector<void*> params;
+    for (int i = 0; i < nbuf; ++i) params.push_back(&ptrs[i]);
+    params.push_back(&dimblk);
+    for (int t = 0; t < ntmaps; ++t) params.push_back(&maps[t]);
+
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    RT_CHECK(cudaSetDevice(dev));
+    if (time_ms) {
+        RT_CHECK(cudaEventCreate(&e0));
+        RT_CHECK(cudaEventCreate(&e1));
+        RT_CHECK(cudaEventRecord(e0, s));
+    }
+    if (cluster_x > 1) {
+        CUlaunchConfig cfg;
+        memset(&cfg, 0, sizeof cfg);
+        cfg.gridDimX = grid[0]; cfg.gridDimY = grid[1]; cfg.gridDimZ = grid[2];
+        cfg.blockDimX = block[0]; cfg.blockDimY = block[1]; cfg.blockDimZ = block[2];
+        cfg.sharedMemBytes = dyn_smem;
+        cfg.hStream = (CUstream)s;
+        CUlaunchAttribute attr;
+        memset(&attr, 0, sizeof attr);
+        attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        attr.value.clusterDim.x = cluster_x;
+        attr.value.clusterDim.y = 1;
+        attr.value.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        DRV_CHECK(LaunchKernelEx(&cfg, f, params.data(), nullptr));
+    } else {
+        DRV_CHECK(LaunchKernel(f, grid[0], grid[1], grid[2], block[0], block[1], block[2], dyn_smem,
+                                 (CUstream)s, params.data(), nullptr));
+    }
+    if (time_ms) {
+        RT_CHECK(cudaEventRecord(e1, s));
+        RT_CHECK(cudaEventSynchronize(e1));
+        RT_CHECK(cudaEventElapsedTime(time_ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    return 0;
+}
+
+int mt_sync(int dev) {
+    cudaStream_t s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_dev(dev)) return 1;
+        s = g_dev[dev].stream;
+    }
+    RT_CHECK(cudaStreamSynchronize(s));
+    RT_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int mt_event_create(uint64_t* ev) {
+    cudaEvent_t e;
+    RT_CHECK(cudaEventCreate(&e));
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t h = g_next++;
+    g_events[h] = e;
+    *ev = h;
+    return 0;
+}
+
+int mt_event_record(int dev, uint64_t ev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    auto it = g_events.find(ev);
+    if (it == g_events.end()) return fail("unknown event");
+    RT_CHECK(cudaEventRecord(it->second, g_dev[dev].stream));
+    return 0;
+}
+
+int mt_event_elapsed(uint64_t start, uint64_t end, float* ms) {
+    cudaEvent_t a, b;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto i = g_events.find(start), j = g_events.find(end);
+        if (i == g_events.end() || j == g_events.end()) return fail("unknown event");
+        a = i->second;
+        b = j->second;
+    }
+    RT_CHECK(cudaEventSynchronize(b));
+    RT_CHECK(cudaEventElapsedTime(ms, a, b));
+    return 0;
+}
+
+int mt_event_destroy(uint64_t ev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_events.find(ev);
+    if (it == g_events.end()) return fail("unknown event");
+    cudaEventDestroy(it->second);
+    g_events.erase(it);
+    return 0;
+}
+
+int mt_graph_begin(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    RT_CHECK(cudaStreamBeginCapture(g_dev[dev].stream, cudaStreamCaptureModeThreadLocal));
+    return 0;
+}
+
+int mt_graph_end(int dev, uint64_t* graph) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    cudaGraph_t g;
+    RT_CHECK(cudaStreamEndCapture(g_dev[dev].stream, &g));
+    cudaGraphExec_t ex;
+    RT_CHECK(cudaGraphInstantiate(&ex, g, 0));
+    cudaGraphDestroy(g);
+    uint64_t h = g_next++;
+    g_graphs[h] = ex;
+    *graph = h;
+    return 0;
+}
+
+int mt_graph_launch(int dev, uint64_t graph) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    auto it = g_graphs.find(graph);
+    if (it == g_graphs.end()) return fail("unknown graph");
+    RT_CHECK(cudaGraphLaunch(it->second, g_dev[dev].stream));
+    return 0;
+}
+
+int mt_graph_destroy(uint64_t graph) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_graphs.find(graph);
+    if (it == g_graphs.end()) return fail("unknown graph");
+    cudaGraphExecDestroy(it->second);
+    g_graphs.erase(it);
+    return 0;
+}
+
+}  // extern "C"

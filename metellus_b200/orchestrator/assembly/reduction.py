@@ -1,0 +1,57 @@
+"""Reduction strategies: standalone, prologue-fused, epilogue-fused last-axis
+reduction (reference template: assembly/reduction.py:24-109). One 256-thread block
+per row; slots: input 0, output 1, chain extras after."""
+
+from __future__ import annotations
+
+from metellus_b200.compute.fragments import CodegenContext
+from metellus_b200.compute.reduction import (
+    LastAxisReductionComputeFragment,
+    LastAxisReductionSetupFragment,
+    StoreReductionResultFragment,
+)
+from metellus_b200.orchestrator.assembly.decision import DecisionView
+from metellus_b200.orchestrator.assembly.expressions import (
+    build_reduction_epilogue_transform,
+    chain_value_transform,
+)
+from metellus_b200.orchestrator.assembly.extras import Extras, param_decl, pname
+from metellus_b200.orchestrator.assembly.matmul import batch_stride_of
+from metellus_b200.orchestrator.ir import ReductionOp, Tensor
+from metellus_b200.orchestrator.kernel_group import KernelGroup
+from metellus_b200.runtime.program import Kernel
+
+RED_THREADS = 256
+
+
+def assemble_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup:
+    anchor = decision.anchor
+    assert isinstance(anchor, ReductionOp)
+    src = decision.prologue_a[0].operands[0] if decision.prologue_a else anchor.input
+    assert isinstance(src, Tensor)
+    M, K = src.matrix_shape
+    batch = src.batch
+    final_out = decision.epilogue[-1].out if decision.epilogue else anchor.out
+    extras = Extras(base_slots_by_key={src.buffer_key: 0, final_out.buffer_key: 1})
+    pro = chain_value_transform(decision.prologue_a, row_var="row", col_var="idx", extras=extras,
+                                base_slot=2) if decision.prologue_a else None
+    epi = build_reduction_epilogue_transform(decision.epilogue) if decision.epilogue else None
+    nt = RED_THREADS
+    frags = (
+        LastAxisReductionSetupFragment(rows_dim="M", name="reduction_setup"),
+        LastAxisReductionComputeFragment(op=anchor.op, input_name=pname(src.buffer_key), scratch_name="scratch",
+                                         reduce_dim="K", row_stride=str(src.row_stride), name="reduction_compute",
+                                         tg_x=nt, col_stride=str(src.col_stride), value_transform=pro),
+        StoreReductionResultFragment(output_name=pname(final_out.buffer_key), scratch_name="scratch",
+                                     name="reduction_store", tg_x=nt, value_transform=epi),
+    )
+    bindings = (src.buffer_key, final_out.buffer_key, *extras.bindings)
+    params = (param_decl(src.buffer_key), param_decl(final_out.buffer_key, writable=True),
+              *extras.buffers)
+    bstrides = (batch_stride_of(src), batch_stride_of(final_out), *extras.batch_strides)
+    fn = function_name or f"reduce_{anchor.out.name}_fused"
+    ctx = CodegenContext(function_name=fn, buffers=params, dims=("M", "K"), tg_x=nt, tg_y=1,
+                         threadgroup_decls=(f"smem float scratch[{(nt + 31) // 32}];",),
+                         batch_strides=bstrides if batch > 1 else ())
+    return KernelGroup(kernel=Kernel(fragments=frags, ctx=ctx), bindings=bindings, dims=(M, K),
+                       grid=(M, 1, batch), threads=(nt, 1, 1), ops=decision.ops, strategy=decision.strategy)

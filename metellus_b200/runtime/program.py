@@ -1,0 +1,194 @@
+"""Host-side runtime steps (reference: src/runtime/program.py:27-215).
+
+``Runtime`` is an ordered list of steps run against an env dict: ``FromNumpy`` /
+``Allocate`` / ``Free`` / ``Upload`` / ``Download`` / ``Fill`` manage buffers,
+``Kernel`` renders (and here also compiles) a kernel, ``Dispatch`` launches it.
+
+CUDA differences: ``Kernel.execute`` compiles through NVRTC and the cubin cache off
+the hot path (the reference's Metal backend recompiled on every ``run_kernel``,
+metal_backend.mm:191); ``Dispatch`` passes dims by value instead of allocating a dims
+buffer per launch (program.py:186) and launches asynchronously — only ``Download``,
+profile timing and explicit syncs wait for the device.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Protocol
+
+import numpy as np
+
+from metellus_b200.compute.fragments import CodegenContext, CodegenEngine, smem_bytes_of
+from metellus_b200.runtime import backend
+from metellus_b200.runtime.buffer import Buffer
+
+Env = dict[str, Any]
+
+
+class RuntimeFragment(Protocol):
+    def execute(self, env: Env) -> None: ...
+
+
+@dataclass(frozen=True)
+class Allocate:
+    name: str
+    nbytes: int
+
+    def execute(self, env: Env) -> None:
+        if self.name in env:
+            raise KeyError(f"Allocate: key {self.name!r} already in env")
+        env[self.name] = Buffer(self.nbytes)
+
+
+@dataclass(frozen=True)
+class Free:
+    name: str
+
+    def execute(self, env: Env) -> None:
+        env.pop(self.name).release()
+
+
+@dataclass(frozen=True)
+class Upload:
+    name: str
+    source: np.ndarray
+
+    def execute(self, env: Env) -> None:
+        env[self.name].write(self.source)
+
+
+@dataclass(frozen=True)
+class FromNumpy:
+    name: str
+    source: np.ndarray
+
+    def execute(self, env: Env) -> None:
+        if self.name in env:
+            raise KeyError(f"FromNumpy: key {self.name!r} already in env")
+        env[self.name] = Buffer.from_numpy(self.source)
+
+
+@dataclass(frozen=True)
+class Download:
+    """Read a buffer into a fresh ndarray at env[into]; with strides, gather a view
+    host-side (program.py:288-335)."""
+
+    name: str
+    shape: tuple[int, ...]
+    dtype: Any
+    into: str
+    row_stride: int | None = None
+    col_stride: int | None = None
+    batch_stride: int | None = None
+
+    def execute(self, env: Env) -> None:
+        buf = env[self.name]
+        if self.row_stride is None:
+            env[self.into] = buf.numpy(self.shape, self.dtype)
+            return
+        item = np.dtype(self.dtype).itemsize
+        flat = buf.numpy((buf.nbytes // item,), self.dtype)
+        if len(self.shape) == 3:
+            st = ((self.batch_stride or 0) * item, self.row_stride * item, (self.col_stride or 0) * item)
+        elif len(self.shape) == 2:
+            st = (self.row_stride * item, (self.col_stride or 0) * item)
+        elif len(self.shape) == 1:
+            st = (self.row_stride * item,)
+        else:
+            raise ValueError(f"Download with strides supports 1D..3D shapes; got {self.shape}")
+        view = np.lib.stride_tricks.as_strided(flat, shape=self.shape, strides=st, writeable=False)
+        env[self.into] = np.ascontiguousarray(view)
+
+
+@dataclass(frozen=True)
+class Fill:
+    name: str
+    byte_value: int = 0
+
+    def execute(self, env: Env) -> None:
+        env[self.name].fill(self.byte_value)
+
+
+class Kernel:
+    """A rendered, lazily compiled CUDA kernel (program.py:126-161)."""
+
+    def __init__(self, fragments: tuple[Any, ...], ctx: CodegenContext) -> None:
+        self.fragments = tuple(fragments)
+        self.ctx = ctx
+        self._source: str | None = None
+        self._handle: int | None = None
+        self._dims_slot_index = ctx.dims_buffer_index if ctx.dims_buffer_index is not None else len(ctx.buffers)
+
+    @property
+    def source(self) -> str:
+        if self._source is None:
+            self._source = CodegenEngine().render(list(self.fragments), self.ctx)
+        return self._source
+
+    @property
+    def function_name(self) -> str:
+        return self.ctx.function_name
+
+    @property
+    def dims_slot_index(self) -> int:
+        return self._dims_slot_index
+
+    @property
+    def dim_names(self) -> tuple[str, ...]:
+        return self.ctx.dims
+
+    @property
+    def smem_bytes(self) -> int:
+        """Dynamic shared memory the launch needs (arena of all tile decls)."""
+        return smem_bytes_of(self.ctx)
+
+    @property
+    def handle(self) -> int:
+        if self._handle is None:
+            self._handle = backend.load_kernel(self.source, self.function_name)
+        return self._handle
+
+    def execute(self, env: Env) -> None:
+        _ = self.handle
+
+
+@dataclass(frozen=True)
+class Dispatch:
+    """Launch a Kernel with env buffers in binding order (program.py:164-197)."""
+
+    kernel: Kernel
+    bindings: tuple[str, ...]
+    dims: tuple[int, ...]
+    grid: tuple[int, int, int]
+    threads: tuple[int, int, int]
+    time_key: str | None = None
+    tmaps: tuple = ()
+    cluster_x: int = 1
+
+    def execute(self, env: Env) -> None:
+        if len(self.dims) != len(self.kernel.dim_names):
+            raise ValueError(
+                f"Dispatch: expected {len(self.kernel.dim_names)} dim values "
+                f"({self.kernel.dim_names}), got {len(self.dims)}"
+            )
+        handles = [env[name].handle for name in self.bindings]
+        t = backend.launch(self.kernel.handle, handles, self.dims, self.grid, self.threads,
+                           smem=self.kernel.smem_bytes, tmaps=self.tmaps, cluster_x=self.cluster_x,
+                           timed=self.time_key is not None)
+        if self.time_key is not None:
+            env[self.time_key] = float(t)
+
+
+@dataclass(frozen=True)
+class Runtime:
+    fragments: tuple[RuntimeFragment, ...] = field(default_factory=tuple)
+
+    def run(self, env: Env | None = None) -> Env:
+        if env is None:
+            env = {}
+        for f in self.fragments:
+            f.execute(env)
+        return env
+
+    def __add__(self, other: "Runtime") -> "Runtime":
+        return Runtime(self.fragments + other.fragments)
