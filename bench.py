@@ -57,6 +57,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--shape", default="", help="override the per-GPU shape, e.g. M=2048,N=8192 "
+                   "(profiling captures on a smaller case)")
     return p.parse_args()
 
 
@@ -239,6 +241,9 @@ def main() -> None:
     backend.init()
     key = args.config
     shape = shard_shape(key)
+    for kv in filter(None, args.shape.split(",")):
+        k, v = kv.split("=")
+        shape[k] = int(v)
     ops = configs.CONFIGS[key].build(**shape, seed=rank)
     groups = compile_program(ops)
     for g in groups:
@@ -272,9 +277,15 @@ def main() -> None:
     barrier()
     ev = [(backend.Event(), backend.Event()) for _ in range(args.steps)]
     gev = [[(backend.Event(), backend.Event()) for _ in groups] for _ in range(args.steps)]
+    # Clock sampling covers a ~1 s soak of the same steps right before the timed
+    # region and the timed region itself (nvidia-smi samples every 100 ms).
     sampler = ClockSampler(local)
     sampler.start()
-    time.sleep(0.3)
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.0:
+        for _ in range(8):
+            step()
+        backend.sync()
     barrier()
     t_wall = time.perf_counter()
     for i in range(args.steps):
