@@ -7,6 +7,7 @@ typedef unsigned int uint32_t;
 typedef int int32_t;
 typedef unsigned long long uint64_t;
 typedef long long int64_t;
+typedef unsigned long long uintptr_t;
 #ifndef MT_SIZE_T_DEFINED
 #define MT_SIZE_T_DEFINED
 #endif

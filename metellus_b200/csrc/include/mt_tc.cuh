@@ -1,0 +1,529 @@
+// sm_100a tensor-core helpers: mbarriers, TMA, tcgen05 / TMEM, and the 3xTF32 GEMM
+// mainloop used by every tcgen05 matmul group (standalone, with prologue / epilogue,
+// and the two-anchor diamond).
+//
+// 3xTF32: each fp32 operand x is split as hi = round_tf32(x), lo = x - hi
+// and the product is accumulated in fp32 TMEM as hi*hi + hi*lo + lo*hi, which keeps
+// about 22 bits of each operand (fp32 carries 24): normwise error close to an fp32
+// dot product, at tensor-core rate.
+//
+// All spin-waits are bounded by wall time (%globaltimer). On timeout the waiting
+// thread records a code in the kernel's status word, raises the CTA abort flag and
+// returns false; every role then leaves its loop, in-flight copies are drained with
+// a bounded wait, TMEM is freed and the kernel returns. The host reads the status
+// word after the launch and raises.
+#pragma once
+
+#define MT_WAIT_LIMIT_NS 2000000000ull  // 2 s per wait
+
+struct alignas(64) mt_tmap { unsigned long long v[16]; };
+
+__device__ __forceinline__ uint32_t mt_smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t mt_globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- mbarrier ------------------------------------------------------------------
+
+__device__ __forceinline__ void mt_mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(mt_smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mt_fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mt_mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+                 :: "r"(mt_smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mt_mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+                 :: "r"(mt_smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mt_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(mt_smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true when the phase completed, false on timeout or CTA abort.
+__device__ __forceinline__ bool mt_mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                             int* status, int code) {
+    if (mt_mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = mt_globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mt_mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (mt_globaltimer() - t0 > MT_WAIT_LIMIT_NS) {
+                if (status) atomicCAS(status, 0, code);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait that ignores the abort flag: used on the abort path to let this CTA's
+// own in-flight bulk copies land before it exits (0.5 s limit).
+__device__ __forceinline__ void mt_mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = mt_globaltimer();
+    while (!mt_mbar_try_wait(bar, parity)) {
+        if (mt_globaltimer() - t0 > 500000000ull) return;
+    }
+}
+
+// Prologue / epilogue adaptors around lambdas generated per kernel.
+template <class F>
+struct mt_prologue {
+    F f;
+    static constexpr bool kActive = true;
+    __device__ __forceinline__ float operator()(float x, int r, int k) const { return f(x, r, k); }
+};
+template <class F>
+struct mt_epilogue {
+    F f;
+    template <class V>
+    __device__ __forceinline__ void store(int row, int col0, V& v) const { f(row, col0, v); }
+};
+
+// ---- TMA -------------------------------------------------------------------------
+
+__device__ __forceinline__ void mt_tma_prefetch(const mt_tmap* m) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+__device__ __forceinline__ void mt_tma_load_2d(void* dst, const mt_tmap* m, uint64_t* bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        :: "r"(mt_smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(m)), "r"(mt_smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void mt_tma_load_3d(void* dst, const mt_tmap* m, uint64_t* bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        :: "r"(mt_smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(m)), "r"(mt_smem_u32(bar)), "r"(c0), "r"(c1),
+           "r"(c2)
+        : "memory");
+}
+// Generic-proxy writes to shared memory become visible to the async proxy
+// (tcgen05.mma operand reads) after this fence.
+__device__ __forceinline__ void mt_fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- tcgen05 / TMEM ----------------------------------------------------------------
+
+__device__ __forceinline__ void mt_tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(mt_smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mt_tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mt_tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void mt_tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::tf32, one CTA.
+__device__ __forceinline__ void mt_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive on `bar` once all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void mt_mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(mt_smem_u32(bar)) : "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp gets lane (base+t).
+__device__ __forceinline__ void mt_tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout type 2, version 1).
+__device__ __forceinline__ uint64_t mt_sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor for kind::tf32 with fp32 accumulation.
+__host__ __device__ constexpr uint32_t mt_idesc_tf32(int M, int N, bool a_mn_major, bool b_mn_major) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Round an fp32 value to the nearest tf32 (10 explicit mantissa bits, ties to even);
+// the result is an fp32 whose low 13 mantissa bits are zero.
+__device__ __forceinline__ float mt_round_tf32(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
+    u += 0xFFFu + ((u >> 13) & 1u);
+    return __uint_as_float(u & 0xFFFFE000u);
+}
+// hi = round_tf32(x); lo = x - hi exactly (the MMA keeps lo's leading tf32 bits).
+// Exact-arithmetic 3xTF32 error with this split: ~4e-8 normwise on N(0,1) data.
+__device__ __forceinline__ void mt_split_tf32(float x, float& hi, float& lo) {
+    hi = mt_round_tf32(x);
+    lo = __fsub_rn(x, hi);
+}
+
+// ---------------------------------------------------------------------------------
+// The GEMM mainloop.
+//
+// Tile BM=128 rows x BN columns, K chunks of BK=32 fp32 (one 128-byte swizzle row);
+// warp roles are listed at mt_gemm_3xtf32.
+//
+// Operand tiles in shared memory, per stage:
+//   A K-major  : TMA box {32 (k), 128 (m)}, rows of 128 B, 8-row atoms (SBO 1024 B),
+//                MMA k-step of 8 = +32 B.
+//   A MN-major : TMA 3-D box {32 (m), 32 (k), 4 (m/32)}: 32-column chunks of 4 KB
+//                (LBO 4096 B), k rows of 128 B (SBO 1024 B), MMA k-step = +1024 B.
+//   B likewise with n in place of m.
+// ---------------------------------------------------------------------------------
+
+struct mt_gemm_smem_plan {
+    static constexpr uint32_t kBK = 32;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int NB>
+struct mt_gemm_layout {
+    static_assert(!A_MN, "A tiles must be K-major");
+    static constexpr uint32_t kABytes = 128u * 32u * 4u;            // 16 KB
+    static constexpr uint32_t kBBytes = (uint32_t)BN * 32u * 4u;
+    // Per stage: A hi (TMA target, split in place), A lo, then per anchor b:
+    // [B raw (MN-major TMA target) when B_MN], B hi, B lo (K-major).
+    static constexpr uint32_t kBSlots = B_MN ? 3u : 2u;
+    static constexpr uint32_t kStageBytes = 2u * kABytes + (uint32_t)NB * kBSlots * kBBytes;
+    static constexpr uint32_t kTileBytes = STAGES * kStageBytes;
+    static constexpr uint32_t kBarOffset = kTileBytes;              // full, conv, empty per stage + accum
+    static constexpr uint32_t kBytes = kTileBytes + (3 * STAGES + 4) * 8 + 16;
+};
+
+// K-major 128-byte-swizzled operand tile (rows of 32 fp32 = 128 B, 8-row atoms of
+// 1 KB): descriptor for MMA k-step kk (8 tf32 = 32 B into each row).
+//
+// tcgen05 kind::tf32 is only used with K-major operands here: a run with an
+// MN-major (N-contiguous) fp32 B tile described as SWIZZLE_128B left the
+// accumulator unchanged, so N-contiguous B tiles are transposed to K-major by the
+// converter warps instead (they touch every element anyway to split hi / lo).
+__device__ __forceinline__ uint64_t mt_operand_desc_k(uint32_t base, int kk) {
+    return mt_sdesc_sw128(base + (uint32_t)kk * 32u, 16u, 1024u);
+}
+
+// Byte offset of element (row r, k) in a K-major 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t mt_kmajor_off(uint32_t r, uint32_t k) {
+    return r * 128u + ((((k >> 2) ^ (r & 7u)) & 7u) << 4) + ((k & 3u) << 2);
+}
+
+// Coordinates of element `i` (0..rows*32-1 in storage order) of an operand tile:
+// row within the tile (m or n) and k within the chunk, undoing the 128-byte swizzle.
+template <bool MN>
+__device__ __forceinline__ void mt_tile_coord(uint32_t byte_off, int& r, int& k) {
+    const uint32_t line = byte_off >> 7;               // 128-byte line index
+    const uint32_t chunk = ((byte_off >> 4) & 7u) ^ (line & 7u);
+    const uint32_t in = (byte_off >> 2) & 3u;
+    const uint32_t inner = chunk * 4u + in;            // logical position within the 128 B line
+    if (MN) {
+        // line = kk_row + 32 * chunk32 ; inner = column within the 32-wide chunk
+        k = (int)(line & 31u);
+        r = (int)((line >> 5) * 32u + inner);
+    } else {
+        r = (int)line;
+        k = (int)inner;
+    }
+}
+
+// Identity prologue (no transform, no coordinates needed).
+struct mt_no_prologue {
+    static constexpr bool kActive = false;
+    __device__ __forceinline__ float operator()(float x, int, int) const { return x; }
+};
+
+// Split one landed fp32 tile in place: hi overwrites the tile, lo goes to `lo`.
+// `rows` is the tile extent along M (A) or N (B); `r0` / `k0` its global origin;
+// `rlim` / `klim` the global bounds (prologue transforms only touch in-bounds
+// elements; out-of-bounds elements were zero-filled by TMA and stay 0).
+template <bool MN, bool A_SIDE, class Pro>
+__device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int rows, int r0, int k0, int rlim, int klim,
+                                                const Pro& pro, int tid, int nthreads) {
+    const int n4 = rows * 32 / 4;
+    for (int i = tid; i < n4; i += nthreads) {
+        float4 v = reinterpret_cast<float4*>(tile)[i];
+        if constexpr (Pro::kActive) {
+            int r, k;
+            mt_tile_coord<MN>((uint32_t)i * 16u, r, k);
+            const int gr = r0 + r, gk = k0 + k;
+            float* e = reinterpret_cast<float*>(&v);
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                if (gr < rlim && gk + l < klim) {
+                    if constexpr (A_SIDE) e[l] = pro(e[l], gr, gk + l);
+                    else e[l] = pro(e[l], gk + l, gr);
+                }
+            }
+        }
+        float4 h, w;
+        mt_split_tf32(v.x, h.x, w.x);
+        mt_split_tf32(v.y, h.y, w.y);
+        mt_split_tf32(v.z, h.z, w.z);
+        mt_split_tf32(v.w, h.w, w.w);
+        reinterpret_cast<float4*>(tile)[i] = h;
+        reinterpret_cast<float4*>(lo)[i] = w;
+    }
+}
+
+// Split an N-contiguous (MN-major) landed B tile and transpose it into K-major hi /
+// lo tiles. The raw tile holds 32-column chunks of 32 k-rows (4 KB each, 128-byte
+// swizzled rows). Lane t of each warp takes k = t of one 4-column group, so both the
+// swizzled 16-byte reads and the transposed scalar writes are bank-conflict free.
+template <class Pro>
+__device__ __forceinline__ void mt_convert_tile_mn(const float* raw, float* hi, float* lo, int cols, int n0, int k0,
+                                                   int nlim, int klim, const Pro& pro, int warp, int nwarps,
+                                                   int lane) {
+    const uint32_t k = (uint32_t)lane;
+    for (int g = warp; g < cols / 4; g += nwarps) {
+        const uint32_t line = k + 32u * (uint32_t)(g >> 3);
+        const uint32_t cg = (uint32_t)(g & 7);
+        float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const unsigned char*>(raw) + line * 128u +
+                                                    ((cg ^ (k & 7u)) << 4));
+        float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t n = 4u * (uint32_t)g + (uint32_t)l;
+            float x = e[l];
+            if constexpr (Pro::kActive) {
+                if (n0 + (int)n < nlim && k0 + (int)k < klim) x = pro(x, k0 + (int)k, n0 + (int)n);
+            }
+            float h, w;
+            mt_split_tf32(x, h, w);
+            const uint32_t off = mt_kmajor_off(n, k);
+            *reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(hi) + off) = h;
+            *reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(lo) + off) = w;
+        }
+    }
+}
+
+// C-tile = A(128 x K) * B_b(K x BN) for b < NB (NB = 2: two anchors sharing A).
+//
+// 512 threads, 16 warps:
+//   warp 0       TMA producer (one elected lane)
+//   warp 1       TMEM owner + MMA issuer (one elected lane)
+//   warps 2..7   converters: split / transpose each landed stage into tf32 hi / lo
+//   warps 8..15  accumulators + epilogue: warp w owns TMEM lane quarter (w % 4) and
+//                half (w - 8) / 4 of the columns of every anchor.
+//
+// Accuracy: the tensor core's fp32 accumulation loses bits on every add (the error
+// grows linearly with K: ~7e-6 normwise at K = 1024 when one TMEM accumulator runs
+// the whole K loop). So each chunk of CHUNK k-tiles is accumulated into a fresh TMEM
+// buffer (double buffered), and the accumulator warps add every finished chunk into
+// fp32 registers with round-to-nearest adds, which keeps the normwise error at the
+// level of an fp32 dot product.
+template <int BN, int STAGES, bool A_MN, bool B_MN, int NB, class ProA, class ProB, class Epi, int CHUNK = 1>
+__device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
+                                               int M, int N, int K, const ProA& proA, const ProB& proB,
+                                               const Epi& epi, int* status, void* smem_raw) {
+    using L = mt_gemm_layout<BN, STAGES, A_MN, B_MN, NB>;
+    constexpr int HALF = BN / 2;                  // columns per accumulator warp per anchor
+    constexpr uint32_t TCOLS = 2u * NB * BN;      // two chunk buffers
+    constexpr uint32_t NCOLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
+    static_assert(TCOLS <= 512, "accumulators exceed TMEM");
+    static_assert(BN == 64 || BN == 128, "BN must be 64 or 128");
+    static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
+    constexpr int NCONV = 6;
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+    uint64_t* conv = full + STAGES;
+    uint64_t* empty = conv + STAGES;
+    uint64_t* tfull = empty + STAGES;   // [2]
+    uint64_t* tempty = tfull + 2;       // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+    const int m0 = (int)blockIdx.y * 128, n0 = (int)blockIdx.x * BN;
+    const int nk = (K + 31) / 32;
+    const int nchunks = (nk + CHUNK - 1) / CHUNK;
+    auto A_hi = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
+    auto A_lo = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes + L::kABytes); };
+    auto B_slot = [&](int s, int b, int j) {
+        return reinterpret_cast<float*>(smem + s * L::kStageBytes + 2 * L::kABytes +
+                                        (b * L::kBSlots + j) * L::kBBytes);
+    };
+    auto B_dst = [&](int s, int b) { return B_slot(s, b, 0); };
+    auto B_hi = [&](int s, int b) { return B_slot(s, b, B_MN ? 1 : 0); };
+    auto B_lo = [&](int s, int b) { return B_slot(s, b, B_MN ? 2 : 1); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mt_mbar_init(&full[s], 1);
+            mt_mbar_init(&conv[s], NCONV);
+            mt_mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mt_mbar_init(&tfull[b], 1);
+            mt_mbar_init(&tempty[b], 8);
+        }
+        *abort_flag = 0;
+        mt_fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        mt_tma_prefetch(tmA);
+        mt_tma_prefetch(tmB0);
+        if (NB > 1) mt_tma_prefetch(tmB1);
+    }
+    if (warp == 1) mt_tmem_alloc(tmem_slot, NCOLS);
+    mt_tc_fence_before();
+    __syncthreads();
+    mt_tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < nk; ++kt) {
+                const int s = kt % STAGES;
+                const uint32_t round = (uint32_t)(kt / STAGES);
+                if (kt >= STAGES && !mt_mbar_wait(&empty[s], (round - 1) & 1u, abort_flag, status, 1)) break;
+                mt_mbar_expect_tx(&full[s], L::kABytes + NB * L::kBBytes);
+                mt_tma_load_2d(A_hi(s), tmA, &full[s], kt * 32, m0);
+                for (int b = 0; b < NB; ++b) {
+                    const mt_tmap* tb = b == 0 ? tmB0 : tmB1;
+                    if (B_MN) mt_tma_load_3d(B_dst(s, b), tb, &full[s], 0, kt * 32, n0 / 32);
+                    else mt_tma_load_2d(B_dst(s, b), tb, &full[s], kt * 32, n0);
+                }
+                issued = kt + 1;
+            }
+            if (*abort_flag) {  // let this CTA's own copies land before it can exit
+                for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
+                    mt_mbar_drain(&full[kt % STAGES], (uint32_t)(kt / STAGES) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = mt_idesc_tf32(128, BN, false, false);
+            bool ok = true;
+            for (int c = 0; c < nchunks && ok; ++c) {
+                const int tb = c & 1;
+                if (c >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((c >> 1) - 1) & 1u, abort_flag, status, 2)) break;
+                mt_tc_fence_after();
+                const int kt0 = c * CHUNK, kt1 = min(kt0 + CHUNK, nk);
+                for (int kt = kt0; kt < kt1; ++kt) {
+                    const int s = kt % STAGES;
+                    if (!mt_mbar_wait(&conv[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    mt_tc_fence_after();
+                    const uint32_t ah = mt_smem_u32(A_hi(s)), al = mt_smem_u32(A_lo(s));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t dah = mt_operand_desc_k(ah, kk);
+                        const uint64_t dal = mt_operand_desc_k(al, kk);
+#pragma unroll
+                        for (int b = 0; b < NB; ++b) {
+                            const uint32_t d = tmem + (uint32_t)((tb * NB + b) * BN);
+                            const uint64_t dbh = mt_operand_desc_k(mt_smem_u32(B_hi(s, b)), kk);
+                            const uint64_t dbl = mt_operand_desc_k(mt_smem_u32(B_lo(s, b)), kk);
+                            mt_mma_tf32(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
+                            mt_mma_tf32(d, dal, dbh, idesc, 1u);
+                            mt_mma_tf32(d, dah, dbh, idesc, 1u);
+                        }
+                    }
+                    mt_mma_commit(&empty[s]);
+                }
+                mt_mma_commit(&tfull[tb]);
+            }
+        }
+    } else if (warp < 8) {
+        const int cw = warp - 2;                    // converter warp 0..5
+        const int ct = cw * 32 + lane;              // 0..191
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % STAGES;
+            if (!mt_mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 3)) break;
+            mt_convert_tile<false, true>(A_hi(s), A_lo(s), 128, m0, kt * 32, M, K, proA, ct, NCONV * 32);
+            for (int b = 0; b < NB; ++b) {
+                if (B_MN)
+                    mt_convert_tile_mn(B_dst(s, b), B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, cw, NCONV,
+                                       lane);
+                else
+                    mt_convert_tile<false, false>(B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, ct,
+                                                  NCONV * 32);
+            }
+            mt_fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mt_mbar_arrive(&conv[s]);
+        }
+    } else {
+        const int q = warp & 3;                     // TMEM lane quarter
+        const int h = (warp - 8) >> 2;              // column half
+        float acc[NB][HALF];
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int j = 0; j < HALF; ++j) acc[b][j] = 0.0f;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c) {
+            const int tb = c & 1;
+            if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c >> 1) & 1u, abort_flag, status, 5)) {
+                ok = false;
+                break;
+            }
+            mt_tc_fence_after();
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+#pragma unroll
+                for (int j = 0; j < HALF / 32; ++j) {
+                    float v[32];
+                    mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((tb * NB + b) * BN + h * HALF + j * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[b][j * 32 + i] = __fadd_rn(acc[b][j * 32 + i], v[i]);
+                }
+            }
+            mt_tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mt_mbar_arrive(&tempty[tb]);
+        }
+        if (ok) {
+            const int row = m0 + q * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < HALF / 32; ++j) {
+                float v[NB][32];
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[b][i] = acc[b][j * 32 + i];
+                epi.store(row, n0 + h * HALF + j * 32, v);
+            }
+        }
+    }
+    mt_tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        mt_tc_fence_after();
+        mt_tmem_dealloc(tmem, NCOLS);
+    }
+}

@@ -1,12 +1,340 @@
-"""tcgen05 / TMEM 3xTF32 matmul path (B200). Until it is wired in, every matmul
-group takes the SIMT FFMA pipe."""
+"""tcgen05 / TMEM 3xTF32 tensor-core pipe for matmul groups (B200).
+
+Every matmul strategy (standalone, register or shared-tile epilogue, elementwise
+prologue) and the two-anchor strategies (multi-producer convergent, diamond) lower to
+one warp-specialised kernel built on ``mt_gemm_3xtf32`` (csrc/include/mt_tc.cuh):
+
+* TMA (128-byte swizzle) streams 128 x 32 A tiles and BN x 32 B tiles into a ring of
+  shared-memory stages;
+* four converter warps split each landed fp32 tile into tf32 hi / lo in place,
+  applying the prologue chain (read at the element's global (row, k)) first;
+* one thread issues ``tcgen05.mma.kind::tf32`` for hi*lo + lo*hi + hi*hi into fp32
+  TMEM accumulators (one per anchor);
+* the same four warps read the accumulators back with ``tcgen05.ld`` and run the
+  epilogue (the fused elementwise chain, or the two-anchor merge) at each element's
+  global (row, col) and store the result.
+
+The pipe is chosen per group: shapes the tensor maps cannot describe (batched
+operands, unaligned strides, an MN-major operand whose extent is not a multiple of
+32) or tiny problems stay on the SIMT FFMA pipe. ``METELLUS_TC=0`` forces FFMA.
+"""
 
 from __future__ import annotations
 
+import os
+from dataclasses import dataclass
 
-def try_assemble_tc_matmul(decision, function_name):
+from metellus_b200.compute.device_lib import header
+from metellus_b200.compute.elementwise import BroadcastSpec, elementwise_expression
+from metellus_b200.compute.fragments import CodegenContext, TgmemAccess
+from metellus_b200.orchestrator.assembly.decision import DecisionView
+from metellus_b200.orchestrator.assembly.expressions import (
+    chain_value_transform,
+    scalar_literal,
+    substitute,
+    wrap_bool,
+)
+from metellus_b200.orchestrator.assembly.extras import Extras, param_decl, pname
+from metellus_b200.orchestrator.ir import ElementwiseOp, MatmulOp, Scalar, Tensor
+from metellus_b200.orchestrator.kernel_group import STATUS_BYTES, STATUS_KEY, FusionStrategy, KernelGroup
+from metellus_b200.runtime.program import Kernel, TmapSpec
+
+SM_COUNT = 148
+SMEM_BUDGET = 200 * 1024
+MIN_VOLUME = 64 * 64 * 64
+
+
+def tc_enabled() -> bool:
+    return os.environ.get("METELLUS_TC", "1") != "0"
+
+
+def _a_layout(t: Tensor) -> str | None:
+    """'k' (K contiguous), 'mn' (M contiguous) or None when TMA cannot describe it."""
+    if len(t.shape) != 2:
+        return None
+    M, K = t.shape
+    if t.col_stride == 1 and (t.row_stride * 4) % 16 == 0 and (M == 1 or t.row_stride >= K):
+        return "k"
     return None
 
 
-def try_assemble_tc_multi_anchor(decision, function_name):
+def _b_layout(t: Tensor) -> str | None:
+    if len(t.shape) != 2:
+        return None
+    K, N = t.shape
+    if t.col_stride == 1 and (t.row_stride * 4) % 16 == 0 and N % 32 == 0 and t.row_stride >= N:
+        return "mn"
+    if t.row_stride == 1 and (t.col_stride * 4) % 16 == 0 and t.col_stride >= K:
+        return "k"
     return None
+
+
+def _tmap(buf_index: int, t: Tensor, layout: str, outer_box: int) -> TmapSpec:
+    """Tensor map for a 128-byte-swizzled operand tile of 32 k-columns.
+
+    K-major: 2-D {K, rows} box {32, outer_box}. MN-major: 3-D {32, K, rows/32} box
+    {32, 32, outer_box/32} — 32-wide chunks along M/N land 4 KB apart."""
+    R, K = (t.shape[0], t.shape[1])
+    if layout == "k":
+        if t.col_stride == 1:  # A-like: rows along dim 0
+            rows, ld = t.shape[0], t.row_stride
+            kdim = t.shape[1]
+        else:  # B stored K-contiguous: rows are n, ld = col_stride
+            rows, ld = t.shape[1], t.col_stride
+            kdim = t.shape[0]
+        return TmapSpec(buf_index, (kdim, rows), (ld * 4,), (32, outer_box))
+    # MN-major
+    if t.row_stride == 1:  # A col-major: contiguous along M, ld = col_stride
+        rows, ld, kdim = t.shape[0], t.col_stride, t.shape[1]
+    else:  # B row-major: contiguous along N, ld = row_stride
+        rows, ld, kdim = t.shape[1], t.row_stride, t.shape[0]
+    return TmapSpec(buf_index, (32, kdim, rows // 32), (ld * 4, 128), (32, 32, outer_box // 32))
+
+
+def _stage_bytes(bn: int, nb: int, b_mn: bool) -> int:
+    """A hi + A lo, then per anchor (B raw when N-contiguous) + B hi + B lo."""
+    return 2 * 128 * 32 * 4 + nb * (3 if b_mn else 2) * bn * 32 * 4
+
+
+def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True) -> tuple[int, int]:
+    """(BN, stages): the widest N tile that still gives ~one CTA per SM, and as many
+    pipeline stages as fit the shared-memory budget."""
+    tiles_m = -(-M // 128)
+    bn = 128 if nb == 1 and tiles_m * -(-N // 128) >= SM_COUNT * 0.8 else 64
+    stages = max(2, min(4, SMEM_BUDGET // _stage_bytes(bn, nb, b_mn)))
+    return bn, stages
+
+
+def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
+    return stages * _stage_bytes(bn, nb, b_mn) + (3 * stages + 4) * 8 + 16 + 1024
+
+
+def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
+    p = pname(t.buffer_key)
+    rs, cs = t.row_stride, t.col_stride
+    if len(t.matrix_shape) == 1:
+        return f"{p}[(size_t)({row}) * {rs}ll]"
+    if mode is BroadcastSpec.SCALAR:
+        return f"{p}[0]"
+    if mode is BroadcastSpec.ROW:
+        return f"__ldg({p} + (size_t)({col}) * {cs}ll)"
+    if mode is BroadcastSpec.COL:
+        return f"{p}[(size_t)({row}) * {rs}ll]"
+    return f"{p}[(size_t)({row}) * {rs}ll + (size_t)({col}) * {cs}ll]"
+
+
+def epilogue_lines(ops: tuple[ElementwiseOp, ...], acc_names: dict[str, str], row: str, col: str,
+                   suffix: str) -> tuple[list[str], dict[str, str]]:
+    """Per-element statements of an epilogue op list; ``acc_names`` maps anchor
+    outputs to accumulator expressions."""
+    vals = dict(acc_names)
+    lines = []
+    for i, op in enumerate(ops):
+        subs = {}
+        modes = (BroadcastSpec.NONE, op.y_broadcast, op.cond_broadcast)
+        for k, key in enumerate(("x", "y", "cond")[: len(op.operands)]):
+            o = op.operands[k]
+            if isinstance(o, Scalar):
+                subs[key] = f"({scalar_literal(o.value)})"
+            elif o.name in vals:
+                subs[key] = f"({vals[o.name]})"
+            else:
+                subs[key] = f"({_read(o, modes[k], row, col)})"
+        v = f"e{i}{suffix}"
+        lines.append(f"const float {v} = {wrap_bool(op.op, substitute(elementwise_expression(op.op), **subs))};")
+        vals[op.out.name] = v
+    return lines, vals
+
+
+@dataclass(frozen=True)
+class TcGemmFragment:
+    """The whole tcgen05 GEMM: lambdas for prologues / epilogue and the mainloop call."""
+
+    bn: int
+    stages: int
+    a_mn: bool  # always False: A tiles are K-major
+    b_mn: bool
+    nb: int
+    pro_a: str | None           # expression in (x, r, c) or None
+    pro_b: str | None
+    epi_body: str               # body of the per-(row, 32 columns) store lambda
+    name: str = "tc_gemm"
+    kind: str = "compute"
+
+    @property
+    def tgmem_accesses(self) -> tuple[TgmemAccess, ...]:
+        n = _smem_bytes(self.bn, self.stages, self.nb, self.b_mn) // 4
+        return (TgmemAccess("tc_arena", "readwrite", n, (1, n)),)
+
+    def render(self, ctx: CodegenContext) -> str:
+        lines = []
+        for side, expr in (("a", self.pro_a), ("b", self.pro_b)):
+            if expr is None:
+                lines.append(f"const mt_no_prologue pro_{side}{{}};")
+            else:
+                lines.append(f"auto pro_{side}_f = [=](float x, int r, int c) -> float {{ return {expr}; }};")
+                lines.append(f"const mt_prologue<decltype(pro_{side}_f)> pro_{side}{{pro_{side}_f}};")
+        lines.append(f"auto epi_f = [=](int row, int col0, float (&v)[{self.nb}][32]) {{\n{self.epi_body}\n}};")
+        lines.append("const mt_epilogue<decltype(epi_f)> epi{epi_f};")
+        tb1 = "&tm_b1" if self.nb > 1 else "&tm_b0"
+        lines.append(
+            f"mt_gemm_3xtf32<{self.bn}, {self.stages}, {str(self.a_mn).lower()}, {str(self.b_mn).lower()}, "
+            f"{self.nb}>(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);"
+        )
+        return "\n".join(lines)
+
+
+def _store_lines(out_key: str, ldo: int, vals_for_j, N: int, need_col_check: bool) -> str:
+    """Store the 32 columns [col0, col0 + 32) of ``row`` (float4 where possible)."""
+    p = pname(out_key)
+    body = ["if (row >= (int)M) return;"]
+    if need_col_check or ldo % 4 != 0:
+        body.append("#pragma unroll\nfor (int j = 0; j < 32; ++j) {")
+        body.append(f"  if (col0 + j < (int)N) {p}[(size_t)row * {ldo}ull + col0 + j] = {vals_for_j('j')};")
+        body.append("}")
+    else:
+        body.append("if (col0 >= (int)N) return;")
+        body.append(f"float* dst = {p} + (size_t)row * {ldo}ull + col0;")
+        body.append("#pragma unroll\nfor (int j = 0; j < 32; j += 4) {")
+        body.append(f"  float4 o; o.x = {vals_for_j('j')}; o.y = {vals_for_j('j + 1')}; "
+                    f"o.z = {vals_for_j('j + 2')}; o.w = {vals_for_j('j + 3')};")
+        body.append("  *reinterpret_cast<float4*>(dst + j) = o;")
+        body.append("}")
+    return "\n".join(body)
+
+
+def _epi_function(ops, acc_names: dict[str, str], out_key: str, final: str, N: int, ldo: int,
+                  need_col_check: bool) -> str:
+    """Epilogue lambda body: evaluates ``ops`` per element and stores ``final``."""
+    # evaluate per element via a small inline function of j
+    lines, vals = epilogue_lines(ops, acc_names, "row", "col0 + J", "")
+    fn = ["auto elem = [&](int J) -> float {"] + ["  " + l for l in lines] + [f"  return {vals[final]};", "};"]
+    body = "\n".join(fn) + "\n" + _store_lines(out_key, ldo, lambda j: f"elem({j})", N, need_col_check)
+    return body
+
+
+def _common_checks(a_src: Tensor, b_src: Tensor, M: int, N: int, K: int) -> tuple[str, str] | None:
+    if not tc_enabled() or M * N * K < MIN_VOLUME:
+        return None
+    la, lb = _a_layout(a_src), _b_layout(b_src)
+    if la is None or lb is None:
+        return None
+    return la, lb
+
+
+def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) -> KernelGroup | None:
+    anchor = decision.anchor
+    assert isinstance(anchor, MatmulOp)
+    if len(anchor.out.shape) != 2:
+        return None
+    src_a = decision.prologue_a[0].operands[0] if decision.prologue_a else anchor.a
+    src_b = decision.prologue_b[0].operands[0] if decision.prologue_b else anchor.b
+    assert isinstance(src_a, Tensor) and isinstance(src_b, Tensor)
+    M, K = anchor.a.shape
+    N = anchor.b.shape[1]
+    lay = _common_checks(src_a, src_b, M, N, K)
+    if lay is None:
+        return None
+    la, lb = lay
+    final_out = decision.epilogue[-1].out if decision.epilogue else anchor.out
+    out_key = final_out.buffer_key
+
+    in_slots: dict[str, int] = {}
+    for t in (src_a, src_b):
+        if t.buffer_key not in in_slots:
+            in_slots[t.buffer_key] = len(in_slots)
+    out_slot = len(in_slots)
+    base = out_slot + 1
+    extras = Extras(base_slots_by_key={**in_slots, out_key: out_slot})
+    pro_a = chain_value_transform(decision.prologue_a, row_var="r", col_var="c", extras=extras,
+                                  base_slot=base)("x") if decision.prologue_a else None
+    pro_b = chain_value_transform(decision.prologue_b, row_var="r", col_var="c", extras=extras,
+                                  base_slot=base)("x") if decision.prologue_b else None
+    for op in decision.epilogue:
+        for o in op.inputs:
+            if o.name not in {e.out.name for e in decision.epilogue} and o.name != anchor.out.name:
+                extras.add_tensor(o, base)
+    bn, stages = _pick_tile(M, N, 1, lb == "mn")
+    need_col_check = N % 32 != 0
+    epi = _epi_function(decision.epilogue, {anchor.out.name: "v[0][J]"}, out_key,
+                        final_out.name, N, N, need_col_check)
+    bindings = (*in_slots.keys(), out_key, *extras.bindings)
+    params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
+    nparams = len(bindings) + 1
+    tmaps = (
+        _tmap(bindings.index(src_a.buffer_key), src_a, la, 128),
+        _tmap(bindings.index(src_b.buffer_key), src_b, lb, bn),
+    )
+    frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=1, pro_a=pro_a,
+                          pro_b=pro_b, epi_body=epi)
+    n_arena = _smem_bytes(bn, stages, 1, lb == "mn") // 4
+    fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
+    ctx = CodegenContext(
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
+        threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
+        helpers=(header("mt_tc.cuh"),),
+        extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0"),
+        min_blocks_per_sm=1,
+    )
+    del nparams
+    return KernelGroup(
+        kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
+        grid=(-(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
+        strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
+    )
+
+
+def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | None) -> KernelGroup | None:
+    """Two anchors sharing A (diamond): one mainloop, two TMEM accumulators, the merge
+    applied in the epilogue. Other two-anchor shapes stay on the SIMT pipe."""
+    if not decision.shared_a:
+        return None
+    a0, a1 = decision.anchors
+    merge = decision.merge_elem
+    if len(a0.out.shape) != 2 or decision.prologues_b[0] or decision.prologues_b[1]:
+        return None
+    M, K = a0.a.shape
+    N = a0.b.shape[1]
+    if a1.a.shape[1] != K:
+        return None
+    lay = _common_checks(a0.a, a0.b, M, N, K)
+    if lay is None or _b_layout(a1.b) != lay[1]:
+        return None
+    la, lb = lay
+    out_key = merge.out.buffer_key
+    in_keys: list[str] = []
+    for t in (a0.a, a0.b, a1.b):
+        if t.buffer_key not in in_keys:
+            in_keys.append(t.buffer_key)
+    out_slot = len(in_keys)
+    extras = Extras(base_slots_by_key={**{k: i for i, k in enumerate(in_keys)}, out_key: out_slot})
+    for o in merge.inputs:
+        if o.name not in (a0.out.name, a1.out.name):
+            extras.add_tensor(o, out_slot + 1)
+    bn, stages = _pick_tile(M, N, 2, lb == "mn")
+    epi = _epi_function((merge,), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key, merge.out.name,
+                        N, N, N % 32 != 0)
+    bindings = (*in_keys, out_key, *extras.bindings)
+    params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
+    tmaps = (
+        _tmap(bindings.index(a0.a.buffer_key), a0.a, la, 128),
+        _tmap(bindings.index(a0.b.buffer_key), a0.b, lb, bn),
+        _tmap(bindings.index(a1.b.buffer_key), a1.b, lb, bn),
+    )
+    frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=2, pro_a=None, pro_b=None,
+                          epi_body=epi)
+    n_arena = _smem_bytes(bn, stages, 2, lb == "mn") // 4
+    fn = function_name or f"tc_diamond_{merge.out.name}_fused"
+    ctx = CodegenContext(
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
+        threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
+        helpers=(header("mt_tc.cuh"),),
+        extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0",
+                      "const __grid_constant__ mt_tmap tm_b1"),
+        min_blocks_per_sm=1,
+    )
+    return KernelGroup(
+        kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
+        grid=(-(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
+        strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
+    )

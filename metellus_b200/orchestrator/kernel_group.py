@@ -21,6 +21,10 @@ from metellus_b200.orchestrator.ir import Op
 from metellus_b200.runtime.program import Kernel
 
 
+STATUS_KEY = "__mt_status"
+STATUS_BYTES = 64
+
+
 class FusionStrategy(StrEnum):
     STANDALONE_MATMUL = "standalone_matmul"
     STANDALONE_ELEMENTWISE = "standalone_elementwise"
@@ -48,7 +52,10 @@ class KernelGroup:
     values; ``grid``/``threads`` the CUDA launch shape (blocks, threads per block).
     ``pipe`` names the arithmetic pipe of a matmul-bearing group ("ffma" SIMT tiles
     or "tcgen05" 3xTF32 tensor-core tiles); ``tmaps`` lists the TMA tensor maps the
-    backend encodes for the launch (empty for plain kernels)."""
+    backend encodes for the launch (empty for plain kernels); ``scratch`` lists
+    (key, nbytes) buffers the kernel takes after its bindings — zero-initialised
+    device memory owned by the runtime, e.g. the ``STATUS_KEY`` word that bounded
+    waits write on timeout."""
 
     kernel: Kernel
     bindings: tuple[str, ...]
@@ -59,7 +66,8 @@ class KernelGroup:
     strategy: FusionStrategy
     pipe: str = ""
     tmaps: tuple = field(default=())
-    aux: tuple = field(default=())
+    scratch: tuple = field(default=())
+    cluster_x: int = 1
 
     @property
     def outputs(self) -> tuple[str, ...]:

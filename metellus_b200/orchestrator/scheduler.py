@@ -21,6 +21,8 @@ from metellus_b200.orchestrator.dag import build_dag
 from metellus_b200.orchestrator.kernel_group import KernelGroup
 from metellus_b200.runtime.program import (
     Allocate,
+    CheckStatus,
+    Fill,
     Dispatch,
     Download,
     Free,
@@ -31,8 +33,18 @@ from metellus_b200.runtime.program import (
 
 
 def dispatch_of(g: KernelGroup, time_key: str | None = None) -> Dispatch:
-    return Dispatch(kernel=g.kernel, bindings=g.bindings, dims=g.dims, grid=g.grid, threads=g.threads,
-                    time_key=time_key, tmaps=g.tmaps, cluster_x=getattr(g, "cluster_x", 1) or 1)
+    """Launch step of a group: parameters are its bindings then its scratch buffers."""
+    keys = tuple(g.bindings) + tuple(k for k, _ in g.scratch)
+    return Dispatch(kernel=g.kernel, bindings=keys, dims=g.dims, grid=g.grid, threads=g.threads,
+                    time_key=time_key, tmaps=g.tmaps, cluster_x=g.cluster_x or 1)
+
+
+def scratch_of(groups: tuple[KernelGroup, ...]) -> dict[str, int]:
+    out: dict[str, int] = {}
+    for g in groups:
+        for k, n in g.scratch:
+            out[k] = max(out.get(k, 0), n)
+    return out
 
 
 def buffer_sizes(ops: Operations, groups: tuple[KernelGroup, ...]) -> dict[str, int]:
@@ -44,8 +56,8 @@ def buffer_sizes(ops: Operations, groups: tuple[KernelGroup, ...]) -> dict[str, 
     for name in ops.uploads:
         sizes[tensors[name].buffer_key] = tensors[name].nbytes
     for g in groups:
-        for key, nbytes in getattr(g, "scratch", ()):
-            sizes[key] = nbytes
+        for key, nbytes in g.scratch:
+            sizes[key] = max(sizes.get(key, 0), nbytes)
     return sizes
 
 
@@ -87,6 +99,10 @@ def schedule(ops: Operations, groups: tuple[KernelGroup, ...], *, profile: bool 
     steps: list[RuntimeFragment] = []
     for name, arr in uploads.items():
         steps.append(FromNumpy(name=tensors[name].buffer_key, source=arr))
+    scratch = scratch_of(groups)
+    for k, n in scratch.items():
+        steps.append(Allocate(name=k, nbytes=n))
+        steps.append(Fill(name=k, byte_value=0))
     seen = set(input_keys)
     for g in groups:
         for k in g.bindings:
@@ -112,4 +128,7 @@ def schedule(ops: Operations, groups: tuple[KernelGroup, ...], *, profile: bool 
             else:
                 steps.append(Free(name=k))
             freed.add(k)
+    for k in scratch:
+        steps.append(CheckStatus(name=k))
+        steps.append(Free(name=k))
     return Runtime(tuple(steps))

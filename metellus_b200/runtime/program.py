@@ -101,6 +101,56 @@ class Download:
 
 
 @dataclass(frozen=True)
+class TmapSpec:
+    """A TMA tensor map the backend encodes at launch (fp32 elements).
+
+    ``buf_index`` indexes the launch's buffer list; ``dims`` / ``box`` are innermost
+    first, ``strides`` are byte strides of dims 1.. ; ``swizzle`` 0/1/2/3 = none /
+    32B / 64B / 128B."""
+
+    buf_index: int
+    dims: tuple[int, ...]
+    strides: tuple[int, ...]
+    box: tuple[int, ...]
+    swizzle: int = 3
+    l2_promo: int = 2
+
+    def to_ctypes(self):
+        s = backend.MtTmapSpec()
+        s.buf_index = self.buf_index
+        s.rank = len(self.dims)
+        for i, d in enumerate(self.dims):
+            s.dims[i] = d
+            s.box[i] = self.box[i]
+            s.elem_strides[i] = 1
+        for i, st in enumerate(self.strides):
+            s.strides[i] = st
+        s.swizzle = self.swizzle
+        s.l2_promo = self.l2_promo
+        s.byte_offset = 0
+        return s
+
+
+@dataclass(frozen=True)
+class CheckStatus:
+    """Read a kernel status word; nonzero means a bounded wait in a kernel timed out
+    (the kernel returned early and its outputs are invalid)."""
+
+    name: str
+
+    def execute(self, env: Env) -> None:
+        buf = env.get(self.name)
+        if buf is None:
+            return
+        words = buf.numpy((buf.nbytes // 4,), np.int32)
+        if words.any():
+            raise RuntimeError(
+                f"kernel status {words[:4].tolist()}: a device-side wait timed out "
+                "(1=producer, 2=mma, 3=converter, 4=epilogue); results are invalid"
+            )
+
+
+@dataclass(frozen=True)
 class Fill:
     name: str
     byte_value: int = 0

@@ -1,0 +1,88 @@
+"""GPU parity of matmul groups on both pipes (tcgen05 3xTF32 and SIMT FFMA) against
+the fp64 oracle: normwise relative error <= 1e-5 and no worse than 4x the fp32 oracle
+(tests/tolerances.py). Covers aligned and ragged M / N / K, a transposed-view B
+(K^T, K-major B tiles), an A-side prologue, shared-tile epilogues and the diamond."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from metellus_b200 import Operations, run
+from oracle.ir_eval import evaluate
+from tests.tolerances import assert_matmul_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _mm(M, K, N, *, bias=False, relu=False, transpose_b=False, prologue=False, seed=0):
+    r = np.random.default_rng(seed)
+    A = r.normal(0, 1, (M, K)).astype(np.float32)
+    ops = Operations()
+    ops.from_numpy(A, "A")
+    if transpose_b:
+        Bt = r.normal(0, 1, (N, K)).astype(np.float32)
+        ops.from_numpy(Bt, "Bt")
+        ops.transpose("Bt", out="B")
+    else:
+        ops.from_numpy(r.normal(0, 1, (K, N)).astype(np.float32), "B")
+    a = "A"
+    if prologue:
+        ops.elementwise("max", out="Ar", operands=("A", -0.5))
+        a = "Ar"
+    ops.matmul(a=a, b="B", out="C")
+    last = "C"
+    if bias:
+        ops.from_numpy(r.normal(0, 1, (1, N)).astype(np.float32), "bias")
+        ops.elementwise("add", out="Cb", operands=("C", "bias"), y_broadcast="row")
+        last = "Cb"
+    if relu:
+        ops.elementwise("max", out="Y", operands=(last, 0.0))
+        last = "Y"
+    return ops, last
+
+
+CASES = [
+    dict(M=256, K=256, N=256),
+    dict(M=1024, K=1024, N=1024, bias=True, relu=True),
+    dict(M=200, K=100, N=96),            # ragged M and K
+    dict(M=128, K=64, N=100, transpose_b=True),   # K-major B, N not a multiple of 32
+    dict(M=384, K=512, N=256, transpose_b=True, bias=True),
+    dict(M=256, K=96, N=160, prologue=True, relu=True),
+]
+
+
+@pytest.mark.parametrize("pipe", ["tcgen05", "ffma"])
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(str(c[k]) for k in "MKN") + "".join(
+    k[0] for k, v in c.items() if v is True))
+def test_matmul_pipes(cuda_device, monkeypatch, pipe, case):
+    monkeypatch.setenv("METELLUS_TC", "1" if pipe == "tcgen05" else "0")
+    ops, out = _mm(**case)
+    res = run(ops)
+    assert len(res.groups) == 1
+    if pipe == "tcgen05":
+        assert res.groups[0].pipe == "tcgen05", res.groups[0].pipe
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env[out], r64[out], r32[out], what=f"{pipe} {case}")
+
+
+@pytest.mark.parametrize("pipe", ["tcgen05", "ffma"])
+def test_diamond_shared_a(cuda_device, monkeypatch, pipe):
+    monkeypatch.setenv("METELLUS_TC", "1" if pipe == "tcgen05" else "0")
+    r = np.random.default_rng(5)
+    M, K, N = 512, 256, 384
+    ops = Operations()
+    ops.from_numpy(r.normal(0, 1, (M, K)).astype(np.float32), "A")
+    ops.from_numpy(r.normal(0, 1, (K, N)).astype(np.float32), "B1")
+    ops.from_numpy(r.normal(0, 1, (K, N)).astype(np.float32), "B2")
+    ops.matmul(a="A", b="B1", out="c1")
+    ops.matmul(a="A", b="B2", out="c2")
+    ops.elementwise("mul", out="z", operands=("c1", "c2"))
+    res = run(ops)
+    assert len(res.groups) == 1 and res.groups[0].strategy.value == "diamond_shared"
+    if pipe == "tcgen05":
+        assert res.groups[0].pipe == "tcgen05"
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env["z"], r64["z"], r32["z"], what=f"diamond {pipe}")
