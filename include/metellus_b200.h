@@ -95,6 +95,22 @@ int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf,
 /* Wait for all work on the device's stream. */
 int mt_sync(int dev);
 
+/* ---- native kernels ------------------------------------------------------- */
+
+/* Last-axis reduction of a rows x cols fp32 matrix stored with row stride `ld`
+ * elements (column stride 1): out[r] = op over c of in[r * ld + c], op 0 = sum,
+ * 1 = max, 2 = min, 3 = product. Sum and product accumulate in fp64 and round once
+ * to fp32. Long rows are split across blocks; each block writes an fp64 partial to
+ * scratch and the last block of a row (atomic ticket) combines the partials in a
+ * fixed order, so results are deterministic. The scratch (partials + tickets) comes
+ * from the device's stream-ordered pool and is returned to it after the launch.
+ * Replaces the reference's reduction kernel for few, long rows (a whole-tensor
+ * sum viewed as (1, M*K) runs on ONE threadgroup there:
+ * src/compute/reduction/reduction.py:24-111, src/orchestrator/assembly/
+ * reduction.py:105-106). `time_ms` as in mt_launch. */
+int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, uint64_t cols, uint64_t ld,
+                   int op, float* time_ms);
+
 /* ---- timing and graphs --------------------------------------------------- */
 
 int mt_event_create(uint64_t* ev);

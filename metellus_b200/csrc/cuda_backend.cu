@@ -150,6 +150,114 @@ int get_func(KernelEntry* k, int dev, CUfunction* f) {
 
 }  // namespace
 
+// ---- native split-row reduction ------------------------------------------------
+
+namespace {
+
+constexpr int kRedThreads = 256;
+
+struct RedSum { static __device__ double id() { return 0.0; }
+                static __device__ double op(double a, double b) { return a + b; } };
+struct RedProd { static __device__ double id() { return 1.0; }
+                 static __device__ double op(double a, double b) { return a * b; } };
+struct RedMax { static __device__ double id() { return -__longlong_as_double(0x7ff0000000000000ll); }
+                static __device__ double op(double a, double b) { return fmax(a, b); } };
+struct RedMin { static __device__ double id() { return __longlong_as_double(0x7ff0000000000000ll); }
+                static __device__ double op(double a, double b) { return fmin(a, b); } };
+
+template <class R>
+__device__ double block_reduce(double v, double* sh) {
+    for (int o = 16; o > 0; o >>= 1) v = R::op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    double r = R::id();
+    if (threadIdx.x < 32) {
+        r = (lane < kRedThreads / 32) ? sh[lane] : R::id();
+        for (int o = 16; o > 0; o >>= 1) r = R::op(r, __shfl_xor_sync(0xffffffffu, r, o));
+    }
+    return r;  // valid in thread 0
+}
+
+// grid (splits, rows): block (s, r) reduces columns [s*chunk, min((s+1)*chunk, cols))
+// of row r into partials[r * splits + s]; the last block of the row (ticket) combines
+// the partials in split order and writes out[r].
+template <class R>
+__global__ void __launch_bounds__(kRedThreads) reduce_rows_split(const float* __restrict__ in,
+                                                                 float* __restrict__ out, double* partials,
+                                                                 unsigned* tickets, unsigned long long cols,
+                                                                 unsigned long long ld, unsigned long long chunk) {
+    __shared__ double sh[kRedThreads / 32];
+    __shared__ bool last;
+    const unsigned long long r = blockIdx.y, s = blockIdx.x, splits = gridDim.x;
+    const unsigned long long c0 = s * chunk, c1 = (c0 + chunk < cols) ? c0 + chunk : cols;
+    const float* row = in + r * ld;
+    double acc = R::id();
+    // 16-byte aligned vector body when the row start and c0 allow it
+    unsigned long long c = c0;
+    const bool vec = ((reinterpret_cast<uintptr_t>(row + c0) & 15u) == 0);
+    if (vec) {
+        const unsigned long long n4 = (c1 - c0) / 4;
+        const float4* p4 = reinterpret_cast<const float4*>(row + c0);
+        for (unsigned long long i = threadIdx.x; i < n4; i += kRedThreads) {
+            const float4 v = __ldcs(p4 + i);
+            acc = R::op(acc, R::op(R::op((double)v.x, (double)v.y), R::op((double)v.z, (double)v.w)));
+        }
+        c = c0 + n4 * 4;
+    }
+    for (unsigned long long i = c + threadIdx.x; i < c1; i += kRedThreads) acc = R::op(acc, (double)row[i]);
+    const double part = block_reduce<R>(acc, sh);
+    if (threadIdx.x == 0) {
+        partials[r * splits + s] = part;
+        __threadfence();
+        last = (atomicAdd(&tickets[r], 1u) == (unsigned)(splits - 1));
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    double tot = R::id();
+    for (unsigned long long i = threadIdx.x; i < splits; i += kRedThreads)
+        tot = R::op(tot, ((volatile double*)partials)[r * splits + i]);
+    tot = block_reduce<R>(tot, sh);
+    if (threadIdx.x == 0) {
+        out[r] = (float)tot;
+        tickets[r] = 0;  // ready for the next launch on the same scratch
+    }
+}
+
+// Grid shape for a rows x cols reduction: about 8 blocks per SM in total, at least
+// 4096 columns per block.
+void reduce_plan(unsigned long long rows, unsigned long long cols, int sms, unsigned long long* splits,
+                 unsigned long long* chunk) {
+    unsigned long long want = (unsigned long long)sms * 8ull / (rows ? rows : 1);
+    unsigned long long max_by_len = (cols + 4095) / 4096;
+    unsigned long long sp = want < max_by_len ? want : max_by_len;
+    if (sp < 1) sp = 1;
+    if (sp > 65535) sp = 65535;
+    unsigned long long ch = (cols + sp - 1) / sp;
+    ch = (ch + 3) / 4 * 4;  // keep every split start 16-byte aligned when the row is
+    *chunk = ch;
+    *splits = (cols + ch - 1) / ch;
+}
+
+int launch_reduce(int op, cudaStream_t st, unsigned long long splits, unsigned long long rows, const float* in,
+                  float* out, double* partials, unsigned* tickets, unsigned long long cols, unsigned long long ld,
+                  unsigned long long chunk) {
+    dim3 grid((unsigned)splits, (unsigned)rows);
+    switch (op) {
+        case 0: reduce_rows_split<RedSum><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
+        case 1: reduce_rows_split<RedMax><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
+        case 2: reduce_rows_split<RedMin><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
+        case 3: reduce_rows_split<RedProd><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
+        default: return fail("mt_reduce_rows: op %d is not 0..3", op);
+    }
+    RT_CHECK(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+
 extern "C" {
 
 int mt_last_error(char* buf, size_t n) {
@@ -442,6 +550,54 @@ int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf, const
         cudaEventDestroy(e1);
     }
     return 0;
+}
+
+int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, uint64_t cols, uint64_t ld, int op,
+                   float* time_ms) {
+    if (rows == 0 || cols == 0) return fail("mt_reduce_rows: empty matrix (%llu x %llu)",
+                                           (unsigned long long)rows, (unsigned long long)cols);
+    if (rows > 65535) return fail("mt_reduce_rows: %llu rows exceed 65535", (unsigned long long)rows);
+    Buffer bi, bo;
+    cudaStream_t st;
+    cudaMemPool_t pool;
+    int sms = 148;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_dev(dev)) return 1;
+        if (get_buf(in_buf, &bi) || get_buf(out_buf, &bo)) return 1;
+        st = g_dev[dev].stream;
+        pool = g_dev[dev].pool;
+        RT_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    }
+    if (bi.dev != dev || bo.dev != dev) return fail("mt_reduce_rows: buffers are not on device %d", dev);
+    if (((rows - 1) * ld + cols) * sizeof(float) > bi.size) return fail("mt_reduce_rows: input buffer too small");
+    if (rows * sizeof(float) > bo.size) return fail("mt_reduce_rows: output buffer too small");
+    unsigned long long splits, chunk;
+    reduce_plan(rows, cols, sms, &splits, &chunk);
+    void* scratch = nullptr;
+    const size_t pbytes = rows * splits * sizeof(double), tbytes = rows * sizeof(unsigned);
+    RT_CHECK(cudaSetDevice(dev));
+    RT_CHECK(cudaMallocAsync(&scratch, pbytes + tbytes, pool, st));
+    double* partials = (double*)scratch;
+    unsigned* tickets = (unsigned*)((char*)scratch + pbytes);
+    RT_CHECK(cudaMemsetAsync(tickets, 0, tbytes, st));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (time_ms) {
+        RT_CHECK(cudaEventCreate(&e0));
+        RT_CHECK(cudaEventCreate(&e1));
+        RT_CHECK(cudaEventRecord(e0, st));
+    }
+    int rc = launch_reduce(op, st, splits, rows, (const float*)bi.ptr, (float*)bo.ptr, partials, tickets, cols, ld,
+                           chunk);
+    if (time_ms) {
+        RT_CHECK(cudaEventRecord(e1, st));
+        RT_CHECK(cudaEventSynchronize(e1));
+        RT_CHECK(cudaEventElapsedTime(time_ms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    RT_CHECK(cudaFreeAsync(scratch, st));
+    return rc;
 }
 
 int mt_sync(int dev) {

@@ -18,15 +18,42 @@ from metellus_b200.orchestrator.assembly.expressions import (
 from metellus_b200.orchestrator.assembly.extras import Extras, param_decl, pname
 from metellus_b200.orchestrator.assembly.matmul import batch_stride_of
 from metellus_b200.orchestrator.ir import ReductionOp, Tensor
-from metellus_b200.orchestrator.kernel_group import KernelGroup
-from metellus_b200.runtime.program import Kernel
+from metellus_b200.orchestrator.kernel_group import FusionStrategy, KernelGroup
+from metellus_b200.runtime.program import Kernel, NativeKernel
 
 RED_THREADS = 256
+SPLIT_MAX_ROWS = 148       # fewer rows than SMs ...
+SPLIT_MIN_COLS = 1 << 16   # ... and long rows: split each row across many blocks
+
+
+def assemble_split_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup | None:
+    """Few, long rows (a whole-tensor reduction viewed as (1, M*K) is the extreme
+    case): the native split-row kernel of the backend (``mt_reduce_rows``), fp64
+    partials combined deterministically. The reference runs such a reduction on a
+    single threadgroup (assembly/reduction.py:105-106)."""
+    anchor = decision.anchor
+    if decision.strategy is not FusionStrategy.STANDALONE_REDUCTION or len(anchor.input.shape) != 2:
+        return None
+    src = anchor.input
+    M, K = src.shape
+    if M > SPLIT_MAX_ROWS or K < SPLIT_MIN_COLS or src.col_stride != 1 or (M > 1 and src.row_stride < K):
+        return None
+    ld = src.row_stride if M > 1 else K
+    ctx = CodegenContext(function_name=function_name or f"reduce_split_{anchor.out.name}",
+                         buffers=(param_decl(src.buffer_key), param_decl(anchor.out.buffer_key, writable=True)),
+                         dims=("M", "K"), tg_x=256, tg_y=1)
+    kernel = NativeKernel("mt_reduce_rows", (M, K, ld, anchor.op), ctx)
+    return KernelGroup(kernel=kernel, bindings=(src.buffer_key, anchor.out.buffer_key), dims=(M, K),
+                       grid=(0, M, 1), threads=(256, 1, 1), ops=decision.ops, strategy=decision.strategy,
+                       pipe="native")
 
 
 def assemble_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup:
     anchor = decision.anchor
     assert isinstance(anchor, ReductionOp)
+    split = assemble_split_reduction(decision, function_name)
+    if split is not None:
+        return split
     src = decision.prologue_a[0].operands[0] if decision.prologue_a else anchor.input
     assert isinstance(src, Tensor)
     M, K = src.matrix_shape

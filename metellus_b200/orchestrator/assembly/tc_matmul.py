@@ -213,8 +213,17 @@ def _epi_function(ops, acc_names: dict[str, str], out_key: str, final: str, N: i
     return body
 
 
+def _fits_cap(nbytes: int) -> bool:
+    """The tensor-core tiles need ~200 KB of shared memory; under a smaller budget
+    cap (e.g. the reference's 32 KB, used to reproduce its plans) the SIMT pipe is
+    chosen instead."""
+    from metellus_b200.orchestrator import fusion
+
+    return nbytes <= fusion.TGMEM_CAP_BYTES
+
+
 def _common_checks(a_src: Tensor, b_src: Tensor, M: int, N: int, K: int) -> tuple[str, str] | None:
-    if not tc_enabled() or M * N * K < MIN_VOLUME:
+    if not tc_enabled() or M * N * K < MIN_VOLUME or not _fits_cap(SMEM_BUDGET):
         return None
     la, lb = _a_layout(a_src), _b_layout(b_src)
     if la is None or lb is None:

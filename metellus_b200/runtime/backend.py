@@ -57,7 +57,7 @@ EXPORTED = (
     "mt_buffer_write_async", "mt_buffer_read_async", "mt_buffer_fill", "mt_host_alloc",
     "mt_host_free", "mt_nvrtc_compile", "mt_kernel_load", "mt_kernel_info", "mt_launch", "mt_sync",
     "mt_event_create", "mt_event_record", "mt_event_elapsed", "mt_event_destroy",
-    "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy",
+    "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy", "mt_reduce_rows",
 )
 
 
@@ -108,6 +108,7 @@ def lib() -> ctypes.CDLL:
                 "mt_graph_end": [i32, P(u64)],
                 "mt_graph_launch": [i32, u64],
                 "mt_graph_destroy": [u64],
+                "mt_reduce_rows": [i32, u64, u64, u64, u64, u64, i32, P(ctypes.c_float)],
             }
             for name, args in sig.items():
                 fn = getattr(L, name)
@@ -320,6 +321,18 @@ def run_kernel(source: str, function_name: str, buffers, grid, threads, *, dims=
     t = launch(k, handles, tuple(dims), tuple(grid), tuple(threads), smem=smem, tmaps=tmaps,
                cluster_x=cluster_x, timed=timed)
     return {"time_ms": t if t is not None else 0.0}
+
+
+REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "product": 3}
+
+
+def reduce_rows(in_handle: int, out_handle: int, rows: int, cols: int, ld: int, op: str, *,
+                timed: bool = False, dev: int | None = None) -> float | None:
+    """Native split-row reduction (``mt_reduce_rows``): out[r] = op(in[r, :])."""
+    ms = ctypes.c_float(0.0)
+    _check(lib().mt_reduce_rows(_device if dev is None else dev, in_handle, out_handle, rows, cols, ld,
+                                REDUCE_OPS[op], ctypes.byref(ms) if timed else None))
+    return float(ms.value) if timed else None
 
 
 # -- events / graphs -------------------------------------------------------------------

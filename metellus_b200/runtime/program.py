@@ -202,6 +202,35 @@ class Kernel:
         _ = self.handle
 
 
+class NativeKernel(Kernel):
+    """A kernel compiled ahead of time into ``libmetellus_cuda.so`` and launched
+    through its own C-ABI entry point (no NVRTC source). ``entry`` names the
+    backend function; ``params`` its static arguments."""
+
+    def __init__(self, entry: str, params: tuple, ctx: CodegenContext) -> None:
+        super().__init__(fragments=(), ctx=ctx)
+        self.entry = entry
+        self.params = tuple(params)
+
+    @property
+    def source(self) -> str:
+        return f"// native kernel {self.entry}{self.params}\n"
+
+    @property
+    def smem_bytes(self) -> int:
+        return 0
+
+    @property
+    def handle(self) -> int:
+        return 0
+
+    def launch(self, handles: list[int], timed: bool) -> float | None:
+        if self.entry == "mt_reduce_rows":
+            rows, cols, ld, op = self.params
+            return backend.reduce_rows(handles[0], handles[1], rows, cols, ld, op, timed=timed)
+        raise ValueError(f"unknown native kernel {self.entry!r}")
+
+
 @dataclass(frozen=True)
 class Dispatch:
     """Launch a Kernel with env buffers in binding order (program.py:164-197)."""
@@ -222,6 +251,11 @@ class Dispatch:
                 f"({self.kernel.dim_names}), got {len(self.dims)}"
             )
         handles = [env[name].handle for name in self.bindings]
+        if isinstance(self.kernel, NativeKernel):
+            t = self.kernel.launch(handles, self.time_key is not None)
+            if self.time_key is not None:
+                env[self.time_key] = float(t)
+            return
         t = backend.launch(self.kernel.handle, handles, self.dims, self.grid, self.threads,
                            smem=self.kernel.smem_bytes, tmaps=self.tmaps, cluster_x=self.cluster_x,
                            timed=self.time_key is not None)
