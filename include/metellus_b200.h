@@ -111,6 +111,23 @@ int mt_sync(int dev);
 int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, uint64_t cols, uint64_t ld,
                    int op, float* time_ms);
 
+/* Allocation-free variant of mt_reduce_rows (no counterpart in the reference).
+ * For callers that cannot allocate device memory: code running inside another
+ * framework's device-memory budget (e.g. a serving process whose caching allocator
+ * owns the GPU) or a latency-critical loop that must not allocate. It calls no
+ * cudaMalloc / cudaFree: its scratch is a fixed 256 KiB array in this library's device
+ * image (kept on every GPU that loads the library until exit). `in` and `out` are
+ * device pointers owned by the caller; `stream` is a cudaStream_t (NULL = this
+ * library's stream for `dev`, which then must have been initialised by mt_init).
+ * Rejects, with an error message, reductions whose partials do not fit
+ * (rows * splits * 8 + rows * 4 > 256 KiB, splits ~ 8 blocks per SM / rows: a few-row
+ * reduction needs ~10 KB; one-split plans fit up to 21,845 rows).
+ * The first call on a device looks up the array's device address (module set-up):
+ * make it before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU (different streams) race; the tickets are cleared per call. */
+int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, uint64_t cols, uint64_t ld,
+                           int op, void* stream);
+
 /* ---- timing and graphs --------------------------------------------------- */
 
 int mt_event_create(uint64_t* ev);

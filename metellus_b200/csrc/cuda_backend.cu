@@ -258,6 +258,22 @@ int launch_reduce(int op, cudaStream_t st, unsigned long long splits, unsigned l
 
 }  // namespace
 
+// ---- allocation-free variant of mt_reduce_rows -------------------------------------
+//
+// Scratch for mt_reduce_rows_noalloc: one fixed array per device, part of this
+// library's device image, so the entry point never allocates. 256 KiB holds the fp64
+// partials and tickets of any plan with rows * splits * 8 + rows * 4 <= 256 KiB: a
+// whole-tensor or few-row reduction needs about 10 KB (8 blocks per SM in total), and
+// one-split plans fit up to 21,845 rows. Every GPU that loads the library keeps this
+// array until the process exits.
+static constexpr size_t kNoAllocScratchBytes = size_t(256) << 10;
+static __device__ __align__(256) unsigned char mt_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+void* g_noalloc_scratch_ptr[kMaxDev] = {};  // device address of mt_noalloc_scratch per device
+std::mutex g_noalloc_mu;
+}  // namespace
+
 extern "C" {
 
 int mt_last_error(char* buf, size_t n) {
@@ -598,6 +614,59 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
     }
     RT_CHECK(cudaFreeAsync(scratch, st));
     return rc;
+}
+
+// Allocation-free reduction for callers that cannot allocate device memory: code
+// that runs inside another framework's device-memory budget (a serving process whose
+// caching allocator has reserved the GPU, where an extra cudaMalloc can fail or
+// fragment that pool) and latency-critical loops where an allocation may synchronise
+// the device. Same kernel and plan as mt_reduce_rows; the scratch is the static
+// array above. `in` / `out` are device pointers the caller owns (in: (rows - 1) * ld
+// + cols floats, out: rows floats).
+int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, uint64_t cols, uint64_t ld,
+                           int op, void* stream) {
+    if (!in || !out) return fail("mt_reduce_rows_noalloc: null input or output pointer");
+    if (rows == 0 || cols == 0)
+        return fail("mt_reduce_rows_noalloc: empty matrix (%llu x %llu)", (unsigned long long)rows,
+                    (unsigned long long)cols);
+    if (rows > 65535) return fail("mt_reduce_rows_noalloc: %llu rows exceed 65535", (unsigned long long)rows);
+    if (dev < 0 || dev >= kMaxDev) return fail("mt_reduce_rows_noalloc: device index %d out of range", dev);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (!st) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_dev[dev].ready)
+            return fail("mt_reduce_rows_noalloc: no stream given and device %d not initialised "
+                        "(pass a stream or call mt_init first)", dev);
+        st = g_dev[dev].stream;
+    }
+    RT_CHECK(cudaSetDevice(dev));
+    int sms = 148;
+    RT_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    unsigned long long splits, chunk;
+    reduce_plan(rows, cols, sms, &splits, &chunk);
+    const size_t pbytes = rows * splits * sizeof(double);
+    const size_t need = pbytes + rows * sizeof(unsigned);
+    if (need > kNoAllocScratchBytes)
+        return fail("mt_reduce_rows_noalloc: this reduction needs %zu bytes of scratch (rows * splits * 8 + "
+                    "rows * 4 with %llu splits per row); the allocation-free entry point has %zu bytes per device "
+                    "- use mt_reduce_rows", need, splits, kNoAllocScratchBytes);
+    void* base = nullptr;
+    {
+        // Set-up, once per device, with that device current: the host-side name of
+        // the __device__ array is not a device address, so look the address up.
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_scratch_ptr[dev]) {
+            void* p = nullptr;
+            RT_CHECK(cudaGetSymbolAddress(&p, mt_noalloc_scratch));
+            g_noalloc_scratch_ptr[dev] = p;
+        }
+        base = g_noalloc_scratch_ptr[dev];
+    }
+    double* partials = (double*)base;
+    unsigned* tickets = (unsigned*)((char*)base + pbytes);
+    // The array keeps the previous call's contents: the tickets must start at zero.
+    RT_CHECK(cudaMemsetAsync(tickets, 0, rows * sizeof(unsigned), st));
+    return launch_reduce(op, st, splits, rows, in, out, partials, tickets, cols, ld, chunk);
 }
 
 int mt_sync(int dev) {

@@ -58,6 +58,7 @@ EXPORTED = (
     "mt_host_free", "mt_nvrtc_compile", "mt_kernel_load", "mt_kernel_info", "mt_launch", "mt_sync",
     "mt_event_create", "mt_event_record", "mt_event_elapsed", "mt_event_destroy",
     "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy", "mt_reduce_rows",
+    "mt_reduce_rows_noalloc",
 )
 
 
@@ -109,6 +110,8 @@ def lib() -> ctypes.CDLL:
                 "mt_graph_launch": [i32, u64],
                 "mt_graph_destroy": [u64],
                 "mt_reduce_rows": [i32, u64, u64, u64, u64, u64, i32, P(ctypes.c_float)],
+                "mt_reduce_rows_noalloc": [i32, ctypes.c_void_p, ctypes.c_void_p, u64, u64, u64, i32,
+                                           ctypes.c_void_p],
             }
             for name, args in sig.items():
                 fn = getattr(L, name)
