@@ -78,7 +78,7 @@ typedef struct mt_tmap_spec {
     uint64_t strides[4];   /* bytes, for dims 1..rank-1 */
     uint32_t box[5];       /* elements per copy, innermost first */
     uint32_t elem_strides[5];
-    int32_t swizzle;       /* 0 none, 1 32B, 2 64B, 3 128B */
+    int32_t swizzle;       /* 0 none, 1 32B, 2 64B, 3 128B, 4 128B with 32-byte atoms */
     int32_t l2_promo;      /* 0 none, 1 64B, 2 128B, 3 256B */
     uint64_t byte_offset;  /* added to the buffer base address */
 } mt_tmap_spec;

@@ -507,11 +507,12 @@ int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf, const
         const mt_tmap_spec& sp = tmaps[t];
         if (sp.buf_index < 0 || sp.buf_index >= nbuf) return fail("tmap %d: bad buffer index", t);
         static const CUtensorMapSwizzle sw[] = {CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
-                                                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_SWIZZLE_128B};
+                                                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B};
         static const CUtensorMapL2promotion l2[] = {
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_64B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B};
-        if (sp.swizzle < 0 || sp.swizzle > 3 || sp.l2_promo < 0 || sp.l2_promo > 3)
+        if (sp.swizzle < 0 || sp.swizzle > 4 || sp.l2_promo < 0 || sp.l2_promo > 3)
             return fail("tmap %d: bad swizzle / l2 promotion", t);
         cuuint64_t gdim[5], gstr[4];
         cuuint32_t box[5], es[5];

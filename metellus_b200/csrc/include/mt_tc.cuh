@@ -47,7 +47,7 @@ __device__ __forceinline__ void mt_mbar_expect_tx(uint64_t* bar, uint32_t bytes)
 __device__ __forceinline__ bool mt_mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n\t"
                  "selp.b32 %0, 1, 0, p;\n\t}"
                  : "=r"(ok) : "r"(mt_smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
@@ -213,9 +213,9 @@ struct mt_gemm_layout {
     static_assert(!A_MN, "A tiles must be K-major");
     static constexpr uint32_t kABytes = 128u * 32u * 4u;            // 16 KB
     static constexpr uint32_t kBBytes = (uint32_t)BN * 32u * 4u;
-    // Per stage: A hi (TMA target, split in place), A lo, then per anchor b:
-    // [B raw (MN-major TMA target) when B_MN], B hi, B lo (K-major).
-    static constexpr uint32_t kBSlots = B_MN ? 3u : 2u;
+    // Per stage: A hi (TMA target, split in place), A lo, then per anchor b: B hi (TMA
+    // target, split in place), B lo.
+    static constexpr uint32_t kBSlots = 2u;
     static constexpr uint32_t kStageBytes = 2u * kABytes + (uint32_t)NB * kBSlots * kBBytes;
     static constexpr uint32_t kTileBytes = STAGES * kStageBytes;
     static constexpr uint32_t kBarOffset = kTileBytes;              // full, conv, empty per stage + accum
@@ -225,18 +225,22 @@ struct mt_gemm_layout {
 // K-major 128-byte-swizzled operand tile (rows of 32 fp32 = 128 B, 8-row atoms of
 // 1 KB): descriptor for MMA k-step kk (8 tf32 = 32 B into each row).
 //
-// tcgen05 kind::tf32 is only used with K-major operands here: a run with an
-// MN-major (N-contiguous) fp32 B tile described as SWIZZLE_128B left the
-// accumulator unchanged, so N-contiguous B tiles are transposed to K-major by the
-// converter warps instead (they touch every element anyway to split hi / lo).
 __device__ __forceinline__ uint64_t mt_operand_desc_k(uint32_t base, int kk) {
     return mt_sdesc_sw128(base + (uint32_t)kk * 32u, 16u, 1024u);
 }
 
-// Byte offset of element (row r, k) in a K-major 128-byte-swizzled tile.
-__device__ __forceinline__ uint32_t mt_kmajor_off(uint32_t r, uint32_t k) {
-    return r * 128u + ((((k >> 2) ^ (r & 7u)) & 7u) << 4) + ((k & 3u) << 2);
+// N-contiguous (MN-major) B tile, as TMA writes it with SWIZZLE_128B_ATOM_32B from a
+// 3-D box {32 (n), 32 (k), BN/32}: 128-byte rows of 32 n-values, one row per k;
+// 32-byte chunks swizzled within 4-row atoms (512 B, SBO); 32-column chunks 4 KB
+// apart (LBO). tf32 MN-major operands use this layout (sm_100 layout type 1,
+// 128-byte swizzle on a 32-byte base); with the plain 128-byte swizzle a B200 run
+// left the accumulator unchanged. MMA k-step kk = 8 rows = +1024 B.
+__device__ __forceinline__ uint64_t mt_operand_desc_mn(uint32_t base, int kk) {
+    const uint32_t a = base + (uint32_t)kk * 1024u;
+    return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)((4096u >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((512u >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (1ull << 61);
 }
+
 
 // Coordinates of element `i` (0..rows*32-1 in storage order) of an operand tile:
 // row within the tile (m or n) and k within the chunk, undoing the 128-byte swizzle.
@@ -295,43 +299,12 @@ __device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int rows
     }
 }
 
-// Split an N-contiguous (MN-major) landed B tile and transpose it into K-major hi /
-// lo tiles. The raw tile holds 32-column chunks of 32 k-rows (4 KB each, 128-byte
-// swizzled rows). Lane t of each warp takes k = t of one 4-column group, so both the
-// swizzled 16-byte reads and the transposed scalar writes are bank-conflict free.
-template <class Pro>
-__device__ __forceinline__ void mt_convert_tile_mn(const float* raw, float* hi, float* lo, int cols, int n0, int k0,
-                                                   int nlim, int klim, const Pro& pro, int warp, int nwarps,
-                                                   int lane) {
-    const uint32_t k = (uint32_t)lane;
-    for (int g = warp; g < cols / 4; g += nwarps) {
-        const uint32_t line = k + 32u * (uint32_t)(g >> 3);
-        const uint32_t cg = (uint32_t)(g & 7);
-        float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const unsigned char*>(raw) + line * 128u +
-                                                    ((cg ^ (k & 7u)) << 4));
-        float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int l = 0; l < 4; ++l) {
-            const uint32_t n = 4u * (uint32_t)g + (uint32_t)l;
-            float x = e[l];
-            if constexpr (Pro::kActive) {
-                if (n0 + (int)n < nlim && k0 + (int)k < klim) x = pro(x, k0 + (int)k, n0 + (int)n);
-            }
-            float h, w;
-            mt_split_tf32(x, h, w);
-            const uint32_t off = mt_kmajor_off(n, k);
-            *reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(hi) + off) = h;
-            *reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(lo) + off) = w;
-        }
-    }
-}
-
 // C-tile = A(128 x K) * B_b(K x BN) for b < NB (NB = 2: two anchors sharing A).
 //
 // 512 threads, 16 warps:
 //   warp 0       TMA producer (one elected lane)
 //   warp 1       TMEM owner + MMA issuer (one elected lane)
-//   warps 2..7   converters: split / transpose each landed stage into tf32 hi / lo
+//   warps 2..7   converters: split each landed stage into tf32 hi / lo in place
 //   warps 8..15  accumulators + epilogue: warp w owns TMEM lane quarter (w % 4) and
 //                half (w - 8) / 4 of the columns of every anchor.
 //
@@ -374,8 +347,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                                         (b * L::kBSlots + j) * L::kBBytes);
     };
     auto B_dst = [&](int s, int b) { return B_slot(s, b, 0); };
-    auto B_hi = [&](int s, int b) { return B_slot(s, b, B_MN ? 1 : 0); };
-    auto B_lo = [&](int s, int b) { return B_slot(s, b, B_MN ? 2 : 1); };
+    auto B_hi = [&](int s, int b) { return B_slot(s, b, 0); };
+    auto B_lo = [&](int s, int b) { return B_slot(s, b, 1); };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -424,7 +397,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = mt_idesc_tf32(128, BN, false, false);
+            constexpr uint32_t idesc = mt_idesc_tf32(128, BN, false, B_MN);
             bool ok = true;
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int tb = c & 1;
@@ -446,8 +419,10 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 #pragma unroll
                         for (int b = 0; b < NB; ++b) {
                             const uint32_t d = tmem + (uint32_t)((tb * NB + b) * BN);
-                            const uint64_t dbh = mt_operand_desc_k(mt_smem_u32(B_hi(s, b)), kk);
-                            const uint64_t dbl = mt_operand_desc_k(mt_smem_u32(B_lo(s, b)), kk);
+                            const uint64_t dbh = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_hi(s, b)), kk)
+                                                      : mt_operand_desc_k(mt_smem_u32(B_hi(s, b)), kk);
+                            const uint64_t dbl = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_lo(s, b)), kk)
+                                                      : mt_operand_desc_k(mt_smem_u32(B_lo(s, b)), kk);
                             mt_mma_tf32(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
                             mt_mma_tf32(d, dal, dbh, idesc, 1u);
                             mt_mma_tf32(d, dah, dbh, idesc, 1u);
@@ -465,14 +440,10 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
             const int s = kt % STAGES;
             if (!mt_mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 3)) break;
             mt_convert_tile<false, true>(A_hi(s), A_lo(s), 128, m0, kt * 32, M, K, proA, ct, NCONV * 32);
-            for (int b = 0; b < NB; ++b) {
-                if (B_MN)
-                    mt_convert_tile_mn(B_dst(s, b), B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, cw, NCONV,
-                                       lane);
-                else
-                    mt_convert_tile<false, false>(B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, ct,
-                                                  NCONV * 32);
-            }
+            // The split is elementwise, so it runs in place whatever the swizzle; the
+            // prologue (coordinates) is only supported on K-major B tiles.
+            for (int b = 0; b < NB; ++b)
+                mt_convert_tile<false, false>(B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, ct, NCONV * 32);
             mt_fence_proxy_async();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(&conv[s]);

@@ -88,12 +88,13 @@ def _tmap(buf_index: int, t: Tensor, layout: str, outer_box: int) -> TmapSpec:
         rows, ld, kdim = t.shape[0], t.col_stride, t.shape[1]
     else:  # B row-major: contiguous along N, ld = row_stride
         rows, ld, kdim = t.shape[1], t.row_stride, t.shape[0]
-    return TmapSpec(buf_index, (32, kdim, rows // 32), (ld * 4, 128), (32, 32, outer_box // 32))
+    # 128-byte swizzle on 32-byte atoms: the layout tcgen05 reads tf32 MN-major operands in
+    return TmapSpec(buf_index, (32, kdim, rows // 32), (ld * 4, 128), (32, 32, outer_box // 32), swizzle=4)
 
 
 def _stage_bytes(bn: int, nb: int, b_mn: bool) -> int:
-    """A hi + A lo, then per anchor (B raw when N-contiguous) + B hi + B lo."""
-    return 2 * 128 * 32 * 4 + nb * (3 if b_mn else 2) * bn * 32 * 4
+    """A hi + A lo, then per anchor B hi + B lo (split in place)."""
+    return 2 * 128 * 32 * 4 + nb * 2 * bn * 32 * 4
 
 
 def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True) -> tuple[int, int]:
@@ -245,6 +246,8 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     if lay is None:
         return None
     la, lb = lay
+    if decision.prologue_b and lb == "mn":
+        return None  # prologue coordinates are only decoded for K-major B tiles
     final_out = decision.epilogue[-1].out if decision.epilogue else anchor.out
     out_key = final_out.buffer_key
 
