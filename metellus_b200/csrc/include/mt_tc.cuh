@@ -142,6 +142,15 @@ __device__ __forceinline__ void mt_mma_tf32(uint32_t d_tmem, uint64_t a_desc, ui
                  "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
                  :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// D(tmem) (+)= A(tmem) * B(smem desc), kind::tf32, one CTA. A sits K-major in tensor
+// memory: lane = row (M = 128), one 32-bit column per k.
+__device__ __forceinline__ void mt_mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
 // Arrive on `bar` once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mt_mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
@@ -164,6 +173,26 @@ __device__ __forceinline__ void mt_tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Thread t of the warp writes 32 consecutive fp32 columns of lane (base+t); returns
+// once the writes are done (tcgen05.wait::st).
+__device__ __forceinline__ void mt_tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        :: "r"(taddr),
+           "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+           "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+           "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+           "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+           "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+           "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+           "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+           "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout type 2, version 1).
 __device__ __forceinline__ uint64_t mt_sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
@@ -184,7 +213,9 @@ __device__ __forceinline__ float mt_round_tf32(float x) {
     return __uint_as_float(u & 0xFFFFE000u);
 }
 // hi = round_tf32(x); lo = x - hi exactly (the MMA keeps lo's leading tf32 bits).
-// Exact-arithmetic 3xTF32 error with this split: ~4e-8 normwise on N(0,1) data.
+// Rounding hi to nearest (rather than letting the MMA truncate x) halves |lo| and so
+// quarters the lo*lo term that 3xTF32 omits: truncated hi measured 4.5e-7 normwise at
+// 4096^3 against 3.2e-7 for this split (fp32 dot products: 3.7e-7).
 __device__ __forceinline__ void mt_split_tf32(float x, float& hi, float& lo) {
     hi = mt_round_tf32(x);
     lo = __fsub_rn(x, hi);
@@ -213,10 +244,10 @@ struct mt_gemm_layout {
     static_assert(!A_MN, "A tiles must be K-major");
     static constexpr uint32_t kABytes = 128u * 32u * 4u;            // 16 KB
     static constexpr uint32_t kBBytes = (uint32_t)BN * 32u * 4u;
-    // Per stage: A hi (TMA target, split in place), A lo, then per anchor b: B hi (TMA
-    // target, split in place), B lo.
+    // Per stage: A (TMA target; its tf32 hi / lo split goes to tensor memory), then per
+    // anchor b: B hi (TMA target, split in place), B lo.
     static constexpr uint32_t kBSlots = 2u;
-    static constexpr uint32_t kStageBytes = 2u * kABytes + (uint32_t)NB * kBSlots * kBBytes;
+    static constexpr uint32_t kStageBytes = kABytes + (uint32_t)NB * kBSlots * kBBytes;
     static constexpr uint32_t kTileBytes = STAGES * kStageBytes;
     static constexpr uint32_t kBarOffset = kTileBytes;              // full, conv, empty per stage + accum
     static constexpr uint32_t kBytes = kTileBytes + (3 * STAGES + 4) * 8 + 16;
@@ -270,17 +301,30 @@ struct mt_no_prologue {
 // `rows` is the tile extent along M (A) or N (B); `r0` / `k0` its global origin;
 // `rlim` / `klim` the global bounds (prologue transforms only touch in-bounds
 // elements; out-of-bounds elements were zero-filled by TMA and stay 0).
-template <bool MN, bool A_SIDE, class Pro>
-__device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int rows, int r0, int k0, int rlim, int klim,
-                                                const Pro& pro, int tid, int nthreads) {
-    const int n4 = rows * 32 / 4;
-    for (int i = tid; i < n4; i += nthreads) {
-        float4 v = reinterpret_cast<float4*>(tile)[i];
+// Convert one landed tile in two phases so every shared-memory load of the thread is
+// in flight before the first split (the converter is latency bound otherwise): load
+// this thread's IT float4 chunks, then apply the prologue (global coordinates
+// recovered from the swizzled offset), split, and store hi in place and lo.
+template <bool MN, bool A_SIDE, int ROWS, int NT, class Pro>
+__device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int r0, int k0, int rlim, int klim,
+                                                const Pro& pro, int tid) {
+    constexpr int N4 = ROWS * 32 / 4;
+    constexpr int IT = (N4 + NT - 1) / NT;
+    float4 v[IT];
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+        const int i = tid + j * NT;
+        if (N4 % NT == 0 || i < N4) v[j] = reinterpret_cast<const float4*>(tile)[i];
+    }
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+        const int i = tid + j * NT;
+        if (!(N4 % NT == 0 || i < N4)) continue;
         if constexpr (Pro::kActive) {
             int r, k;
             mt_tile_coord<MN>((uint32_t)i * 16u, r, k);
             const int gr = r0 + r, gk = k0 + k;
-            float* e = reinterpret_cast<float*>(&v);
+            float* e = reinterpret_cast<float*>(&v[j]);
 #pragma unroll
             for (int l = 0; l < 4; ++l) {
                 if (gr < rlim && gk + l < klim) {
@@ -290,13 +334,47 @@ __device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int rows
             }
         }
         float4 h, w;
-        mt_split_tf32(v.x, h.x, w.x);
-        mt_split_tf32(v.y, h.y, w.y);
-        mt_split_tf32(v.z, h.z, w.z);
-        mt_split_tf32(v.w, h.w, w.w);
+        mt_split_tf32(v[j].x, h.x, w.x);
+        mt_split_tf32(v[j].y, h.y, w.y);
+        mt_split_tf32(v[j].z, h.z, w.z);
+        mt_split_tf32(v[j].w, h.w, w.w);
         reinterpret_cast<float4*>(tile)[i] = h;
         reinterpret_cast<float4*>(lo)[i] = w;
     }
+}
+
+// Split this thread's row of a landed K-major A tile (row q*32+lane: 32 k values in
+// one 128-byte line, 16-byte chunks swizzled by row & 7) into tf32 hi / lo and write
+// them to tensor memory: hi to columns [0, 32) and lo to [32, 64) past `t_hi`, lane =
+// row. Conflict-free: 8 consecutive rows cover all 8 chunk positions.
+template <class Pro>
+__device__ __forceinline__ void mt_convert_a_rows(const float* tile, uint32_t t_hi, int q, int lane, int m0, int k0,
+                                                  int M, int K, const Pro& pro) {
+    const int r = q * 32 + lane;
+    const float4* line = reinterpret_cast<const float4*>(tile + r * 32);
+    float hi[32], lo[32];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float4 x = line[c ^ (r & 7)];
+        hi[4 * c] = x.x;
+        hi[4 * c + 1] = x.y;
+        hi[4 * c + 2] = x.z;
+        hi[4 * c + 3] = x.w;
+    }
+    if constexpr (Pro::kActive) {
+        const int gr = m0 + r;
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            if (gr < M && k0 + k < K) hi[k] = pro(hi[k], gr, k0 + k);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        const float x = hi[k];
+        mt_split_tf32(x, hi[k], lo[k]);
+    }
+    const uint32_t t = t_hi + ((uint32_t)(q * 32) << 16);
+    mt_tmem_st32(t, hi);
+    mt_tmem_st32(t + 32u, lo);
 }
 
 // C-tile = A(128 x K) * B_b(K x BN) for b < NB (NB = 2: two anchors sharing A).
@@ -304,7 +382,10 @@ __device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int rows
 // 512 threads, 16 warps:
 //   warp 0       TMA producer (one elected lane)
 //   warp 1       TMEM owner + MMA issuer (one elected lane)
-//   warps 2..7   converters: split each landed stage into tf32 hi / lo in place
+//   warps 2..7   converters: warps 4..7 split the A rows of their TMEM lane quarter
+//                into tf32 hi / lo in tensor memory (the MMA reads A from there, so
+//                shared memory carries only the TMA write and one read of A); then
+//                all six split the B tiles into hi / lo in place
 //   warps 8..15  accumulators + epilogue: warp w owns TMEM lane quarter (w % 4) and
 //                half (w - 8) / 4 of the columns of every anchor.
 //
@@ -320,9 +401,10 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                                                const Epi& epi, int* status, void* smem_raw) {
     using L = mt_gemm_layout<BN, STAGES, A_MN, B_MN, NB>;
     constexpr int HALF = BN / 2;                  // columns per accumulator warp per anchor
-    constexpr uint32_t TCOLS = 2u * NB * BN;      // two chunk buffers
+    constexpr uint32_t ACOLS = 2u * NB * BN;      // two chunk buffers of accumulators
+    constexpr uint32_t TCOLS = ACOLS + 64u * STAGES;  // + A hi / lo per stage
     constexpr uint32_t NCOLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
-    static_assert(TCOLS <= 512, "accumulators exceed TMEM");
+    static_assert(TCOLS <= 512, "accumulators and A stages exceed TMEM");
     static_assert(BN == 64 || BN == 128, "BN must be 64 or 128");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
     constexpr int NCONV = 6;
@@ -340,10 +422,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     const int m0 = (int)blockIdx.y * 128, n0 = (int)blockIdx.x * BN;
     const int nk = (K + 31) / 32;
     const int nchunks = (nk + CHUNK - 1) / CHUNK;
-    auto A_hi = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
-    auto A_lo = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes + L::kABytes); };
+    auto A_raw = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
     auto B_slot = [&](int s, int b, int j) {
-        return reinterpret_cast<float*>(smem + s * L::kStageBytes + 2 * L::kABytes +
+        return reinterpret_cast<float*>(smem + s * L::kStageBytes + L::kABytes +
                                         (b * L::kBSlots + j) * L::kBBytes);
     };
     auto B_dst = [&](int s, int b) { return B_slot(s, b, 0); };
@@ -382,7 +463,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                 const uint32_t round = (uint32_t)(kt / STAGES);
                 if (kt >= STAGES && !mt_mbar_wait(&empty[s], (round - 1) & 1u, abort_flag, status, 1)) break;
                 mt_mbar_expect_tx(&full[s], L::kABytes + NB * L::kBBytes);
-                mt_tma_load_2d(A_hi(s), tmA, &full[s], kt * 32, m0);
+                mt_tma_load_2d(A_raw(s), tmA, &full[s], kt * 32, m0);
                 for (int b = 0; b < NB; ++b) {
                     const mt_tmap* tb = b == 0 ? tmB0 : tmB1;
                     if (B_MN) mt_tma_load_3d(B_dst(s, b), tb, &full[s], 0, kt * 32, n0 / 32);
@@ -411,11 +492,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                         break;
                     }
                     mt_tc_fence_after();
-                    const uint32_t ah = mt_smem_u32(A_hi(s)), al = mt_smem_u32(A_lo(s));
+                    const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)s;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t dah = mt_operand_desc_k(ah, kk);
-                        const uint64_t dal = mt_operand_desc_k(al, kk);
+                        const uint32_t dah = ah + 8u * (uint32_t)kk;
+                        const uint32_t dal = dah + 32u;
 #pragma unroll
                         for (int b = 0; b < NB; ++b) {
                             const uint32_t d = tmem + (uint32_t)((tb * NB + b) * BN);
@@ -423,9 +504,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                                                       : mt_operand_desc_k(mt_smem_u32(B_hi(s, b)), kk);
                             const uint64_t dbl = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_lo(s, b)), kk)
                                                       : mt_operand_desc_k(mt_smem_u32(B_lo(s, b)), kk);
-                            mt_mma_tf32(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
-                            mt_mma_tf32(d, dal, dbh, idesc, 1u);
-                            mt_mma_tf32(d, dah, dbh, idesc, 1u);
+                            mt_mma_tf32_ts(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
+                            mt_mma_tf32_ts(d, dal, dbh, idesc, 1u);
+                            mt_mma_tf32_ts(d, dah, dbh, idesc, 1u);
                         }
                     }
                     mt_mma_commit(&empty[s]);
@@ -439,12 +520,14 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         for (int kt = 0; kt < nk; ++kt) {
             const int s = kt % STAGES;
             if (!mt_mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 3)) break;
-            mt_convert_tile<false, true>(A_hi(s), A_lo(s), 128, m0, kt * 32, M, K, proA, ct, NCONV * 32);
+            if (warp >= 4)
+                mt_convert_a_rows(A_raw(s), tmem + ACOLS + 64u * (uint32_t)s, warp & 3, lane, m0, kt * 32, M, K, proA);
             // The split is elementwise, so it runs in place whatever the swizzle; the
             // prologue (coordinates) is only supported on K-major B tiles.
             for (int b = 0; b < NB; ++b)
-                mt_convert_tile<false, false>(B_hi(s, b), B_lo(s, b), BN, n0, kt * 32, N, K, proB, ct, NCONV * 32);
+                mt_convert_tile<false, false, BN, NCONV * 32>(B_hi(s, b), B_lo(s, b), n0, kt * 32, N, K, proB, ct);
             mt_fence_proxy_async();
+            mt_tc_fence_before();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(&conv[s]);
         }

@@ -93,16 +93,19 @@ def _tmap(buf_index: int, t: Tensor, layout: str, outer_box: int) -> TmapSpec:
 
 
 def _stage_bytes(bn: int, nb: int, b_mn: bool) -> int:
-    """A hi + A lo, then per anchor B hi + B lo (split in place)."""
-    return 2 * 128 * 32 * 4 + nb * 2 * bn * 32 * 4
+    """A (its hi / lo split lives in tensor memory), then per anchor B hi + B lo
+    (split in place)."""
+    return 128 * 32 * 4 + nb * 2 * bn * 32 * 4
 
 
 def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True) -> tuple[int, int]:
     """(BN, stages): the widest N tile that still gives ~one CTA per SM, and as many
-    pipeline stages as fit the shared-memory budget."""
+    pipeline stages as fit the shared-memory budget and tensor memory (512 columns:
+    two accumulator chunks of nb * BN columns, plus 64 columns of A hi / lo per stage)."""
     tiles_m = -(-M // 128)
     bn = 128 if nb == 1 and tiles_m * -(-N // 128) >= SM_COUNT * 0.8 else 64
-    stages = max(2, min(4, SMEM_BUDGET // _stage_bytes(bn, nb, b_mn)))
+    tmem_stages = (512 - 2 * nb * bn) // 64
+    stages = max(2, min(6, tmem_stages, SMEM_BUDGET // _stage_bytes(bn, nb, b_mn)))
     return bn, stages
 
 
