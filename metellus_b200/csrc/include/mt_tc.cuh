@@ -204,20 +204,21 @@ __host__ __device__ constexpr uint32_t mt_idesc_tf32(int M, int N, bool a_mn_maj
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// Round an fp32 value to the nearest tf32 (10 explicit mantissa bits, ties to even);
-// the result is an fp32 whose low 13 mantissa bits are zero.
-__device__ __forceinline__ float mt_round_tf32(float x) {
-    uint32_t u = __float_as_uint(x);
-    if ((u & 0x7F800000u) == 0x7F800000u) return x;  // inf / nan unchanged
-    u += 0xFFFu + ((u >> 13) & 1u);
-    return __uint_as_float(u & 0xFFFFE000u);
-}
-// hi = round_tf32(x); lo = x - hi exactly (the MMA keeps lo's leading tf32 bits).
-// Rounding hi to nearest (rather than letting the MMA truncate x) halves |lo| and so
-// quarters the lo*lo term that 3xTF32 omits: truncated hi measured 4.5e-7 normwise at
-// 4096^3 against 3.2e-7 for this split (fp32 dot products: 3.7e-7).
+// Veltkamp's splitting (T. J. Dekker, "A floating-point technique for extending the
+// available precision", Numer. Math. 18, 1971) with constant 2^13 + 1: hi carries the
+// leading 24 - 13 = 11 significant bits of x rounded to nearest, so it is exact as a
+// tf32, and lo = x - hi is exact with at most 12 significant bits (the MMA's truncating
+// read keeps 11 of them). Four fp32 operations on the FMA pipe and none on the integer
+// pipe (a bit-mask rounding spends ~7 integer ops per element, and the converter
+// warps were integer-pipe bound with it). Rounding hi to nearest rather than letting
+// the MMA truncate x halves |lo| and quarters the lo*lo term that 3xTF32 omits
+// (truncated hi measured 4.5e-7 normwise at 4096^3, nearest 3.2e-7; fp32 dot products
+// 3.7e-7). Where the product overflows (|x| > ~4e34, or x inf / NaN) hi falls back
+// to x with its low 13 mantissa bits cleared.
 __device__ __forceinline__ void mt_split_tf32(float x, float& hi, float& lo) {
-    hi = mt_round_tf32(x);
+    const float t = __fmul_rn(x, 8193.0f);
+    const float h = __fsub_rn(t, __fsub_rn(t, x));
+    hi = fabsf(t) <= 3.402823466e38f ? h : __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
     lo = __fsub_rn(x, hi);
 }
 
