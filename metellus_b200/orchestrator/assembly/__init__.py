@@ -23,7 +23,8 @@ _ELEMENTWISE = {
     FusionStrategy.ELEMENTWISE_CHAIN,
     FusionStrategy.ELEMENTWISE_DAG,
 }
-_MULTI = {FusionStrategy.MULTI_PRODUCER_CONVERGENT, FusionStrategy.DIAMOND_SHARED}
+_MULTI = {FusionStrategy.MULTI_PRODUCER_CONVERGENT, FusionStrategy.DIAMOND_SHARED,
+          FusionStrategy.DUAL_GEMM_EPILOGUE}
 
 
 def assemble(vertex: Vertex, *, function_name: str | None = None) -> KernelGroup:

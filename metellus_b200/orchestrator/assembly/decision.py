@@ -4,7 +4,8 @@ The reference shapes (single matmul / reduction anchor with a traced prologue ch
 and an epilogue chain, two-anchor merge, elementwise chain, shape copy) classify
 exactly as in the reference. Vertices that only the B200 passes build classify into
 the B200 strategies: a non-chain elementwise DAG -> ELEMENTWISE_DAG; reductions mixed
-with full-row elementwise ops -> ROW_RESIDENT; matmul + reductions -> FUSED_ATTENTION.
+with full-row elementwise ops -> ROW_RESIDENT; matmul + reductions -> FUSED_ATTENTION;
+two matmuls sharing A with an elementwise DAG over both -> DUAL_GEMM_EPILOGUE.
 """
 
 from __future__ import annotations
@@ -98,19 +99,24 @@ def classify(vertex: Vertex) -> DecisionView:
         assert len(matmuls) == 2, "multi-anchor vertex must have exactly 2 matmul anchors"
         a0, a1 = matmuls
         i0, i1 = ops.index(a0), ops.index(a1)
-        post = ops[max(i0, i1) + 1:]
-        assert len(post) == 1 and isinstance(post[0], ElementwiseOp), \
-            "multi-anchor vertex has exactly one merge elem"
-        merge = post[0]
         pre0 = tuple(op for op in ops[:i0] if isinstance(op, ElementwiseOp))
         pre1 = tuple(op for op in ops[:i1] if isinstance(op, ElementwiseOp))
         pa = (trace_prologue(a0.a.name, pre0), trace_prologue(a1.a.name, pre1))
         pb = (trace_prologue(a0.b.name, pre0), trace_prologue(a1.b.name, pre1))
         absorbed = {id(op) for ch in (*pa, *pb) for op in ch}
-        for op in ops:
-            if isinstance(op, ElementwiseOp) and op is not merge:
-                assert id(op) in absorbed, f"pre-anchor op {op.out.name!r} not absorbed by any prologue"
+        post = tuple(op for op in ops if isinstance(op, ElementwiseOp) and id(op) not in absorbed)
         shared = a0.a.name == a1.a.name and a0.a.shape == a1.a.shape and not pa[0] and not pa[1]
+        if len(post) > 1 or (post and ops.index(post[0]) < max(i0, i1)):
+            # B200 dual GEMM: both anchors read one A; an elementwise DAG over the two
+            # accumulators (and other full-shape / broadcast tensors) is the epilogue.
+            assert shared and not absorbed and len(outs) == 1, \
+                "dual-GEMM vertex: shared A, no prologues, one output"
+            final = next(op for op in post if op.out.name == outs[0])
+            return DecisionView(strategy=FusionStrategy.DUAL_GEMM_EPILOGUE, anchors=matmuls, merge_elem=final,
+                                shared_a=True, prologues_a=((), ()), prologues_b=((), ()), epilogue=post,
+                                ops=ops, outputs=outs)
+        assert len(post) == 1, "multi-anchor vertex has exactly one merge elem"
+        merge = post[0]
         return DecisionView(
             strategy=FusionStrategy.DIAMOND_SHARED if shared else FusionStrategy.MULTI_PRODUCER_CONVERGENT,
             anchors=matmuls, merge_elem=merge, shared_a=shared, prologues_a=pa, prologues_b=pb,

@@ -35,6 +35,9 @@ def assemble_multi_anchor(decision: DecisionView, function_name: str | None) -> 
     tc = try_assemble_tc_multi_anchor(decision, function_name)
     if tc is not None:
         return tc
+    if decision.epilogue:
+        raise ValueError("dual-GEMM vertex: the tcgen05 assembly rejected it (the fusion pass "
+                         "only builds one when the tensor-core path accepts the anchors)")
     a0, a1 = decision.anchors
     merge = decision.merge_elem
     assert merge is not None

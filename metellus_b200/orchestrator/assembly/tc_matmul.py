@@ -299,13 +299,26 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     )
 
 
+def dual_gemm_eligible(a0: MatmulOp, a1: MatmulOp) -> bool:
+    """Whether two anchors sharing A can run as one tcgen05 kernel (2-D, same K and
+    N, tensor-map-able operands with one B layout)."""
+    if len(a0.out.shape) != 2 or a0.out.shape != a1.out.shape or a0.a.name != a1.a.name:
+        return False
+    M, K = a0.a.shape
+    N = a0.b.shape[1]
+    lay = _common_checks(a0.a, a0.b, M, N, K)
+    return lay is not None and _b_layout(a1.b) == lay[1]
+
+
 def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | None) -> KernelGroup | None:
     """Two anchors sharing A (diamond): one mainloop, two TMEM accumulators, the merge
+    (or, for a dual-GEMM vertex, the whole elementwise DAG over both accumulators)
     applied in the epilogue. Other two-anchor shapes stay on the SIMT pipe."""
     if not decision.shared_a:
         return None
     a0, a1 = decision.anchors
     merge = decision.merge_elem
+    epi_ops = decision.epilogue or (merge,)
     if len(a0.out.shape) != 2 or decision.prologues_b[0] or decision.prologues_b[1]:
         return None
     M, K = a0.a.shape
@@ -323,12 +336,14 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
             in_keys.append(t.buffer_key)
     out_slot = len(in_keys)
     extras = Extras(base_slots_by_key={**{k: i for i, k in enumerate(in_keys)}, out_key: out_slot})
-    for o in merge.inputs:
-        if o.name not in (a0.out.name, a1.out.name):
-            extras.add_tensor(o, out_slot + 1)
+    inside = {a0.out.name, a1.out.name} | {op.out.name for op in epi_ops}
+    for op in epi_ops:
+        for o in op.inputs:
+            if o.name not in inside:
+                extras.add_tensor(o, out_slot + 1)
     bn, stages = _pick_tile(M, N, 2, lb == "mn")
-    epi = _epi_function((merge,), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key, merge.out.name,
-                        N, N, N % 32 != 0)
+    epi = _epi_function(tuple(epi_ops), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key,
+                        merge.out.name, N, N, N % 32 != 0)
     bindings = (*in_keys, out_key, *extras.bindings)
     params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
     tmaps = (

@@ -97,6 +97,17 @@ def _anchor_of(vertex: Vertex) -> Op | None:
     return None
 
 
+def _is_dual_gemm_vertex(vertex: Vertex) -> bool:
+    """A vertex built by ``try_dual_gemm_fuse``; its tcgen05 template takes no
+    prologues, so the reference prologue passes leave it alone."""
+    if sum(isinstance(op, MatmulOp) for op in vertex.ops) != 2:
+        return False
+    from metellus_b200.orchestrator.assembly.decision import classify
+    from metellus_b200.orchestrator.kernel_group import FusionStrategy
+
+    return classify(vertex).strategy is FusionStrategy.DUAL_GEMM_EPILOGUE
+
+
 def _is_elementwise_vertex(vertex: Vertex) -> bool:
     return len(vertex.ops) > 0 and all(isinstance(op, ElementwiseOp) for op in vertex.ops)
 
@@ -206,7 +217,7 @@ def try_prologue_absorb_single(graph: Graph, blacklist: frozenset[frozenset[int]
             continue
         a = cons[0]
         anchors = [op for op in a.ops if isinstance(op, (MatmulOp, ReductionOp))]
-        if not anchors:
+        if not anchors or _is_dual_gemm_vertex(a):
             continue
         names: set[str] = set()
         for anc in anchors:
@@ -272,7 +283,7 @@ def try_prologue_absorb_multi(graph: Graph, blacklist: frozenset[frozenset[int]]
         ok = True
         for c in cons:
             ac = _anchor_of(c)
-            if ac is None or out not in _anchor_boundary_input_names(ac, c):
+            if ac is None or _is_dual_gemm_vertex(c) or out not in _anchor_boundary_input_names(ac, c):
                 ok = False
                 break
             ids.append(id(ac))
@@ -440,12 +451,75 @@ def try_elementwise_dag_fuse(graph: Graph, blacklist: frozenset[frozenset[int]])
     return None
 
 
+def _elementwise_region(graph: Graph, start: list[Vertex], shape: tuple[int, ...]) -> list[Vertex] | None:
+    """Grow ``start`` by every elementwise vertex over ``shape`` that consumes a tensor
+    the region produces; the region qualifies when exactly one of its tensors is read
+    outside it (or is a program output) and that tensor is an elementwise result."""
+    region = list(start)
+    ids = {id(v) for v in region}
+    grown = True
+    while grown:
+        grown = False
+        for v in list(region):
+            for name in v.outputs:
+                for c in graph.consumers_of(name):
+                    if id(c) in ids or not _is_elementwise_vertex(c):
+                        continue
+                    if any(op.out.shape != shape for op in c.ops):
+                        continue
+                    region.append(c)
+                    ids.add(id(c))
+                    grown = True
+    produced = {op.out.name: op for v in region for op in v.ops}
+    escaping = set()
+    for name in produced:
+        if name in graph.program_outputs or any(id(c) not in ids for c in graph.consumers_of(name)):
+            escaping.add(name)
+    if len(escaping) != 1:
+        return None
+    final = produced[next(iter(escaping))]
+    return region if isinstance(final, ElementwiseOp) else None
+
+
+def try_dual_gemm_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) -> Graph | None:
+    """Two matmuls reading the same A whose outputs meet in an elementwise DAG with a
+    single result (a gated MLP's ``act(H @ W1 + b1) * (H @ W3)``): one tcgen05 kernel
+    streams A once into two TMEM accumulators and evaluates the whole DAG in its
+    epilogue, so neither product nor any intermediate reaches HBM. Runs before the
+    reference passes, which would otherwise split the DAG into epilogues, separate
+    elementwise kernels and a prologue of the next matmul."""
+    from metellus_b200.orchestrator.assembly.tc_matmul import dual_gemm_eligible
+
+    mms = [v for v in graph.vertices if len(v.ops) == 1 and isinstance(v.ops[0], MatmulOp)]
+    for i, p0 in enumerate(mms):
+        for p1 in mms[i + 1:]:
+            a0, a1 = p0.ops[0], p1.ops[0]
+            if not dual_gemm_eligible(a0, a1):
+                continue
+            if any(graph.consumers_of(a.out.name) == () or a.out.name in graph.program_outputs
+                   for a in (a0, a1)):
+                continue
+            region = _elementwise_region(graph, [p0, p1], a0.out.shape)
+            if region is None or len(region) == 2:
+                continue
+            if frozenset(o for v in region for o in v.op_ids) in blacklist:
+                continue
+            try:
+                g = graph.replace(absorbed=tuple(region), ops=_merge_in_order(graph, *region))
+            except ValueError:
+                continue
+            if _views_ordered(g):
+                return g
+    return None
+
+
 def try_attention_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) -> Graph | None:
     from metellus_b200.orchestrator.assembly.attention import match_attention
 
     return match_attention(graph, blacklist)
 
 
+B200_FIRST_PASSES = (try_dual_gemm_fuse,)
 REFERENCE_PASSES = (
     try_elem_chain_fuse,
     try_multi_producer_fuse,
@@ -458,7 +532,7 @@ B200_PASSES = (
     try_row_fuse,
     try_elementwise_dag_fuse,
 )
-_PASSES = REFERENCE_PASSES + B200_PASSES
+_PASSES = B200_FIRST_PASSES + REFERENCE_PASSES + B200_PASSES
 
 
 # ---------------------------------------------------------------------------

@@ -42,6 +42,7 @@ class FusionStrategy(StrEnum):
     ELEMENTWISE_DAG = "elementwise_dag"
     ROW_RESIDENT = "row_resident"
     FUSED_ATTENTION = "fused_attention"
+    DUAL_GEMM_EPILOGUE = "dual_gemm_epilogue"
 
 
 @dataclass(frozen=True)

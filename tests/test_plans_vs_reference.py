@@ -74,3 +74,22 @@ def test_budget_gate_splits_at_small_cap(monkeypatch):
 def test_expected_b200_kernel_counts():
     counts = {n: len(_plan(n, b200=True)) for n in ("c1", "c2", "c3", "c3sum")}
     assert counts == {"c1": 1, "c2": 1, "c3": 1, "c3sum": 1}
+
+
+def test_c5_b200_plan_is_layernorm_dual_gemm_down_projection():
+    """The gated MLP: one row kernel (LayerNorm), one dual GEMM whose epilogue is the
+    whole GELU-gate DAG (writes U only), one GEMM with bias + residual epilogue."""
+    groups = _plan("c5", b200=True)
+    assert [g.strategy.value for g in groups] == ["row_resident", "dual_gemm_epilogue", "matmul_epilogue_tg"]
+    dual = groups[1]
+    assert dual.pipe == "tcgen05"
+    assert [op.out.name for op in dual.ops][-1] == "U"
+    assert "z1b" not in dual.bindings and "g_1" not in dual.bindings
+    assert [op.out.name for op in groups[2].ops] == ["z2", "z2b", "out"]
+
+
+def test_dual_gemm_pass_leaves_reference_diamond_alone():
+    """A bare diamond (merge right after both matmuls) stays the reference's
+    two-anchor vertex; the dual-GEMM pass only fires when an epilogue DAG exists."""
+    groups = _plan("diamond", b200=True)
+    assert len(groups) == 1 and groups[0].strategy.value == "diamond_shared"
