@@ -13,6 +13,10 @@ pass recognises the subgraph
 and fuses it into one flash-style kernel (online softmax over key blocks); the row
 statistics ``mx`` and ``sm`` are still written when the program exposes them. Only the
 S x S intermediates disappear.
+
+Head dim 64 with whole 64-key blocks runs on the tensor cores (tcgen05, 3xTF32,
+``mt_attn_tc.cuh``: TMA-fed K / V blocks, Q and P in tensor memory); other shapes run
+the FFMA kernel (``mt_attn.cuh``).
 """
 
 from __future__ import annotations
@@ -28,7 +32,8 @@ from metellus_b200.orchestrator.assembly.extras import param_decl, pname
 from metellus_b200.orchestrator.graph import Graph
 from metellus_b200.orchestrator.ir import ElementwiseOp, MatmulOp, ReductionOp, Tensor
 from metellus_b200.orchestrator.kernel_group import KernelGroup
-from metellus_b200.runtime.program import Kernel
+from metellus_b200.orchestrator.kernel_group import STATUS_BYTES, STATUS_KEY
+from metellus_b200.runtime.program import Kernel, TmapSpec
 
 
 @dataclass(frozen=True)
@@ -179,6 +184,46 @@ def _smem_floats(d: int) -> int:
     return d * (bq + 4) + d * (bk + 4) + bk * (d + 4) + bk * (bq + 4)
 
 
+@dataclass(frozen=True)
+class TcAttentionFragment:
+    score_expr: str
+    o: str
+    mx: str
+    sm: str
+    sq: int
+    sk: int
+    o_rs: int
+    name: str = "attention_tc"
+    kind: str = "compute"
+
+    @property
+    def tgmem_accesses(self) -> tuple[TgmemAccess, ...]:
+        return (TgmemAccess("attn_arena", "readwrite", TC_ARENA_FLOATS, (1, TC_ARENA_FLOATS)),)
+
+    def render(self, ctx: CodegenContext) -> str:
+        return (
+            f"auto score = [=](float x) -> float {{ return {self.score_expr}; }};\n"
+            f"mt_attn_fwd_tc(&tm_q, &tm_k, &tm_v, {self.o}, {self.mx}, {self.sm}, {self.sq}, {self.sk}, "
+            f"{self.o_rs}ll, score, g_status, attn_arena);"
+        )
+
+
+# mt_fa_layout::kBytes (Q 32 KB + two 64 KB K/V stages + half-row exchange + barriers) plus
+# 1 KB for aligning the arena to the 128-byte swizzle atom.
+TC_ARENA_FLOATS = (32768 + 2 * 65536 + 2048 + 32 * 8 + 16 + 1024) // 4
+
+
+def _tc_attention_ok(Q: Tensor, Kt: Tensor, V: Tensor, O: Tensor, D: int, Sk: int) -> bool:
+    from metellus_b200.orchestrator.assembly.tc_matmul import _fits_cap, tc_enabled
+
+    def bs(t: Tensor) -> int:
+        return t.batch_stride if len(t.shape) == 3 else 0
+
+    aligned = all(x * 4 % 16 == 0 for x in (Q.row_stride, Kt.col_stride, V.row_stride, bs(Q), bs(Kt), bs(V)))
+    return (tc_enabled() and D == 64 and Sk % 64 == 0 and aligned and O.col_stride == 1
+            and O.row_stride % 4 == 0 and _fits_cap(TC_ARENA_FLOATS * 4))
+
+
 def assemble_attention(decision: DecisionView, function_name: str | None) -> KernelGroup:
     m = find_attention(decision.ops)
     if m is None:
@@ -209,6 +254,9 @@ def assemble_attention(decision: DecisionView, function_name: str | None) -> Ker
     if stat_sm:
         strides[stat_sm] = Sq if batched else 0
     score = build_reduction_epilogue_transform(m.score_chain)("x")
+    if _tc_attention_ok(Q, Kt, V, O, D, Sk):
+        return _assemble_tc(decision, m, function_name, bindings, params, strides, batched, B, Sq, Sk, D,
+                            stat_mx, stat_sm, score)
     frag = AttentionFragment(
         d=D, score_expr=score, q=pname(Q.buffer_key), k=pname(Kt.buffer_key), v=pname(V.buffer_key),
         o=pname(O.buffer_key), mx=pname(stat_mx) if stat_mx else "nullptr",
@@ -224,3 +272,39 @@ def assemble_attention(decision: DecisionView, function_name: str | None) -> Ker
     return KernelGroup(kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(B, Sq, D),
                        grid=(-(-Sq // 64), 1, B), threads=(256, 1, 1), ops=decision.ops,
                        strategy=decision.strategy, pipe="ffma")
+
+
+def _assemble_tc(decision, m, function_name, bindings, params, strides, batched, B, Sq, Sk, D, stat_mx, stat_sm,
+                 score) -> KernelGroup:
+    Q, Kt, V, O = m.qk.a, m.qk.b, m.pv.b, m.pv.out
+
+    def bs(t: Tensor, rows: int, rs: int) -> int:
+        return t.batch_stride if len(t.shape) == 3 else rows * rs
+
+    qi, ki, vi = bindings.index(Q.buffer_key), bindings.index(Kt.buffer_key), bindings.index(V.buffer_key)
+    # Q, K: K-major 128-byte-swizzled boxes of 32 d x rows; V: d-contiguous (MN-major for
+    # the P V product) boxes {32 d, 32 keys, 2 d-chunks} on 32-byte swizzle atoms.
+    tmaps = (
+        TmapSpec(qi, (D, Sq, B), (Q.row_stride * 4, bs(Q, Sq, Q.row_stride) * 4), (32, 128, 1)),
+        TmapSpec(ki, (D, Sk, B), (Kt.col_stride * 4, bs(Kt, Sk, Kt.col_stride) * 4), (32, 64, 1)),
+        TmapSpec(vi, (32, Sk, D // 32, B), (V.row_stride * 4, 128, bs(V, Sk, V.row_stride) * 4), (32, 32, 2, 1),
+                 swizzle=4),
+    )
+    frag = TcAttentionFragment(
+        score_expr=score, o=pname(O.buffer_key), mx=pname(stat_mx) if stat_mx else "nullptr",
+        sm=pname(stat_sm) if stat_sm else "nullptr", sq=Sq, sk=Sk, o_rs=O.row_stride,
+    )
+    fn = function_name or f"attention_{O.name}_fused"
+    ctx = CodegenContext(
+        function_name=fn, buffers=params + ("int* g_status",), dims=("B", "S", "D"), tg_x=512, tg_y=1,
+        threadgroup_decls=(f"smem float attn_arena[{TC_ARENA_FLOATS}];",),
+        helpers=(header("mt_tc.cuh"), header("mt_attn_tc.cuh")),
+        extra_params=("const __grid_constant__ mt_tmap tm_q", "const __grid_constant__ mt_tmap tm_k",
+                      "const __grid_constant__ mt_tmap tm_v"),
+        batch_strides=tuple(strides[k] for k in bindings) if batched else (),
+        min_blocks_per_sm=1,
+    )
+    return KernelGroup(kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(B, Sq, D),
+                       grid=(-(-Sq // 128), 1, B), threads=(512, 1, 1), ops=decision.ops,
+                       strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps,
+                       scratch=((STATUS_KEY, STATUS_BYTES),))
