@@ -234,20 +234,23 @@ def main() -> None:
         tdist.init_process_group("nccl", device_id=torch.device("cuda", local))
         dist = tdist
 
+    from metellus_b200 import distributed
     from metellus_b200.api.run import compile_program
     from metellus_b200.orchestrator.scheduler import buffer_sizes, dispatch_of
     from metellus_b200.runtime import backend
     from metellus_b200.runtime.buffer import Buffer
 
-    backend.set_device(local)
-    backend.init()
+    distributed.init()  # binds the GPU; for N > 1 also creates the NCCL communicator
     key = args.config
     shape = shard_shape(key)
     for kv in filter(None, args.shape.split(",")):
         k, v = kv.split("=")
         shape[k] = int(v)
     ops = configs.CONFIGS[key].build(**shape, seed=rank)
-    groups = compile_program(ops)
+    # the whole-tensor sum of a row-sharded X: local fp64 partial + NCCL all-reduce
+    combine = (configs.CONFIGS[key].output,) if key == "c3sum" and world > 1 else ()
+    with distributed.combining(*combine):
+        groups = compile_program(ops)
     for g in groups:
         _ = g.kernel.handle  # compile before timing
     tensors = ops.tensors
@@ -364,6 +367,7 @@ def main() -> None:
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
+        distributed.shutdown()
         dist.destroy_process_group()
 
 

@@ -100,7 +100,8 @@ int mt_sync(int dev);
 /* Last-axis reduction of a rows x cols fp32 matrix stored with row stride `ld`
  * elements (column stride 1): out[r] = op over c of in[r * ld + c], op 0 = sum,
  * 1 = max, 2 = min, 3 = product. Sum and product accumulate in fp64 and round once
- * to fp32. Long rows are split across blocks; each block writes an fp64 partial to
+ * to fp32. Ops 4..7 are the same four with an fp64 `out` (rows doubles): the
+ * per-GPU partial of a sharded whole-tensor reduction, combined by mt_allreduce_f64. Long rows are split across blocks; each block writes an fp64 partial to
  * scratch and the last block of a row (atomic ticket) combines the partials in a
  * fixed order, so results are deterministic. The scratch (partials + tickets) comes
  * from the device's stream-ordered pool and is returned to it after the launch.
@@ -127,6 +128,23 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
  * overlap on the GPU (different streams) race; the tickets are cleared per call. */
 int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, uint64_t cols, uint64_t ld,
                            int op, void* stream);
+
+/* ---- multi-GPU: combining sharded whole-tensor reductions -------------------
+ * No counterpart in the reference (its Metal backend drives one GPU); a sharded
+ * whole-tensor reduction (sum(X) with X's rows split across GPUs) computes one fp64
+ * partial per GPU (mt_reduce_rows op 4..7) and combines the partials with one NCCL
+ * all-reduce over NVLink. One process per GPU; libnccl.so.2 is opened at first use. */
+
+/* NCCL unique id (ncclGetUniqueId) into `out` (cap >= 128 bytes); rank 0 makes it
+ * and the host plumbing (torch.distributed) broadcasts it to the other ranks. */
+int mt_nccl_unique_id(unsigned char* out, uint64_t cap);
+/* Create the device's communicator (ncclCommInitRank): rank `rank` of `nranks`. */
+int mt_nccl_init(int dev, int nranks, int rank, const unsigned char* id);
+int mt_nccl_destroy(int dev);
+/* In-place all-reduce of `count` doubles in `buf` on the device's stream, op 0 = sum,
+ * 1 = max, 2 = min, 3 = product; if `out_f32` is nonzero the result is also written
+ * there rounded to fp32 (the program's output tensor). Stream ordered, no host wait. */
+int mt_allreduce_f64(int dev, uint64_t buf, uint64_t count, int op, uint64_t out_f32);
 
 /* ---- timing and graphs --------------------------------------------------- */
 

@@ -9,6 +9,9 @@
 #include <cuda_runtime.h>
 #include <nvrtc.h>
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -94,6 +97,7 @@ struct Device {
     bool ready = false;
     cudaStream_t stream = nullptr;
     cudaMemPool_t pool = nullptr;
+    ncclComm_t comm = nullptr;  // set by mt_nccl_init
 };
 
 struct Buffer {
@@ -182,10 +186,11 @@ __device__ double block_reduce(double v, double* sh) {
 
 // grid (splits, rows): block (s, r) reduces columns [s*chunk, min((s+1)*chunk, cols))
 // of row r into partials[r * splits + s]; the last block of the row (ticket) combines
-// the partials in split order and writes out[r].
-template <class R>
+// the partials in split order and writes out[r] (fp32, or the fp64 value itself for
+// a partial that another GPU's partials are combined with).
+template <class R, class OutT>
 __global__ void __launch_bounds__(kRedThreads) reduce_rows_split(const float* __restrict__ in,
-                                                                 float* __restrict__ out, double* partials,
+                                                                 OutT* __restrict__ out, double* partials,
                                                                  unsigned* tickets, unsigned long long cols,
                                                                  unsigned long long ld, unsigned long long chunk) {
     __shared__ double sh[kRedThreads / 32];
@@ -221,7 +226,7 @@ __global__ void __launch_bounds__(kRedThreads) reduce_rows_split(const float* __
         tot = R::op(tot, ((volatile double*)partials)[r * splits + i]);
     tot = block_reduce<R>(tot, sh);
     if (threadIdx.x == 0) {
-        out[r] = (float)tot;
+        out[r] = (OutT)tot;
         tickets[r] = 0;  // ready for the next launch on the same scratch
     }
 }
@@ -241,16 +246,23 @@ void reduce_plan(unsigned long long rows, unsigned long long cols, int sms, unsi
     *splits = (cols + ch - 1) / ch;
 }
 
+// op 0..3 = sum / max / min / product with fp32 output; 4..7 the same with fp64 output.
 int launch_reduce(int op, cudaStream_t st, unsigned long long splits, unsigned long long rows, const float* in,
-                  float* out, double* partials, unsigned* tickets, unsigned long long cols, unsigned long long ld,
+                  void* out, double* partials, unsigned* tickets, unsigned long long cols, unsigned long long ld,
                   unsigned long long chunk) {
     dim3 grid((unsigned)splits, (unsigned)rows);
+    float* o32 = (float*)out;
+    double* o64 = (double*)out;
     switch (op) {
-        case 0: reduce_rows_split<RedSum><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
-        case 1: reduce_rows_split<RedMax><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
-        case 2: reduce_rows_split<RedMin><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
-        case 3: reduce_rows_split<RedProd><<<grid, kRedThreads, 0, st>>>(in, out, partials, tickets, cols, ld, chunk); break;
-        default: return fail("mt_reduce_rows: op %d is not 0..3", op);
+        case 0: reduce_rows_split<RedSum><<<grid, kRedThreads, 0, st>>>(in, o32, partials, tickets, cols, ld, chunk); break;
+        case 1: reduce_rows_split<RedMax><<<grid, kRedThreads, 0, st>>>(in, o32, partials, tickets, cols, ld, chunk); break;
+        case 2: reduce_rows_split<RedMin><<<grid, kRedThreads, 0, st>>>(in, o32, partials, tickets, cols, ld, chunk); break;
+        case 3: reduce_rows_split<RedProd><<<grid, kRedThreads, 0, st>>>(in, o32, partials, tickets, cols, ld, chunk); break;
+        case 4: reduce_rows_split<RedSum><<<grid, kRedThreads, 0, st>>>(in, o64, partials, tickets, cols, ld, chunk); break;
+        case 5: reduce_rows_split<RedMax><<<grid, kRedThreads, 0, st>>>(in, o64, partials, tickets, cols, ld, chunk); break;
+        case 6: reduce_rows_split<RedMin><<<grid, kRedThreads, 0, st>>>(in, o64, partials, tickets, cols, ld, chunk); break;
+        case 7: reduce_rows_split<RedProd><<<grid, kRedThreads, 0, st>>>(in, o64, partials, tickets, cols, ld, chunk); break;
+        default: return fail("mt_reduce_rows: op %d is not 0..7", op);
     }
     RT_CHECK(cudaGetLastError());
     return 0;
@@ -588,7 +600,9 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
     }
     if (bi.dev != dev || bo.dev != dev) return fail("mt_reduce_rows: buffers are not on device %d", dev);
     if (((rows - 1) * ld + cols) * sizeof(float) > bi.size) return fail("mt_reduce_rows: input buffer too small");
-    if (rows * sizeof(float) > bo.size) return fail("mt_reduce_rows: output buffer too small");
+    if (op < 0 || op > 7) return fail("mt_reduce_rows: op %d is not 0..7", op);
+    if (rows * (op >= 4 ? sizeof(double) : sizeof(float)) > bo.size)
+        return fail("mt_reduce_rows: output buffer too small");
     unsigned long long splits, chunk;
     reduce_plan(rows, cols, sms, &splits, &chunk);
     void* scratch = nullptr;
@@ -604,7 +618,7 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
         RT_CHECK(cudaEventCreate(&e1));
         RT_CHECK(cudaEventRecord(e0, st));
     }
-    int rc = launch_reduce(op, st, splits, rows, (const float*)bi.ptr, (float*)bo.ptr, partials, tickets, cols, ld,
+    int rc = launch_reduce(op, st, splits, rows, (const float*)bi.ptr, bo.ptr, partials, tickets, cols, ld,
                            chunk);
     if (time_ms) {
         RT_CHECK(cudaEventRecord(e1, st));
@@ -627,6 +641,7 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
 int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, uint64_t cols, uint64_t ld,
                            int op, void* stream) {
     if (!in || !out) return fail("mt_reduce_rows_noalloc: null input or output pointer");
+    if (op < 0 || op > 3) return fail("mt_reduce_rows_noalloc: op %d is not 0..3 (fp32 output)", op);
     if (rows == 0 || cols == 0)
         return fail("mt_reduce_rows_noalloc: empty matrix (%llu x %llu)", (unsigned long long)rows,
                     (unsigned long long)cols);
@@ -668,6 +683,129 @@ int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, 
     // The array keeps the previous call's contents: the tickets must start at zero.
     RT_CHECK(cudaMemsetAsync(tickets, 0, rows * sizeof(unsigned), st));
     return launch_reduce(op, st, splits, rows, in, out, partials, tickets, cols, ld, chunk);
+}
+
+// ---- NCCL: combining whole-tensor reductions across GPUs ------------------------
+//
+// libnccl is opened at first use (dlopen by soname), so the library still loads where
+// NCCL is absent and shares the copy a host framework (torch.distributed) has loaded.
+
+}  // extern "C"
+
+namespace {
+
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+int nccl_api() {
+    std::lock_guard<std::mutex> lk(g_nccl_mu);
+    if (g_nccl.ok) return 0;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail("NCCL: cannot open libnccl.so.2 (%s)", dlerror());
+#define MT_NCCL(name) \
+    g_nccl.name = reinterpret_cast<decltype(g_nccl.name)>(dlsym(h, "nccl" #name)); \
+    if (!g_nccl.name) return fail("NCCL: symbol nccl" #name " missing");
+    MT_NCCL(GetUniqueId)
+    MT_NCCL(CommInitRank)
+    MT_NCCL(AllReduce)
+    MT_NCCL(CommDestroy)
+    MT_NCCL(GetErrorString)
+#undef MT_NCCL
+    g_nccl.ok = true;
+    return 0;
+}
+
+#define NCCL_CHECK(x)                                                                    \
+    do {                                                                                \
+        ncclResult_t r_ = (x);                                                          \
+        if (r_ != ncclSuccess) return fail("%s: %s", #x, g_nccl.GetErrorString(r_));    \
+    } while (0)
+
+__global__ void f64_to_f32(const double* in, float* out, unsigned long long n) {
+    const unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x;
+    if (i < n) out[i] = (float)in[i];
+}
+
+}  // namespace
+
+extern "C" {
+
+int mt_nccl_unique_id(unsigned char* out, uint64_t cap) {
+    if (!out || cap < sizeof(ncclUniqueId)) return fail("mt_nccl_unique_id: buffer below %zu bytes", sizeof(ncclUniqueId));
+    if (nccl_api()) return 1;
+    ncclUniqueId id;
+    NCCL_CHECK(g_nccl.GetUniqueId(&id));
+    memcpy(out, &id, sizeof(id));
+    return 0;
+}
+
+int mt_nccl_init(int dev, int nranks, int rank, const unsigned char* id) {
+    if (!id || nranks < 1 || rank < 0 || rank >= nranks)
+        return fail("mt_nccl_init: rank %d of %d or id invalid", rank, nranks);
+    if (nccl_api()) return 1;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_dev(dev)) return 1;
+        if (g_dev[dev].comm) return fail("mt_nccl_init: device %d already has a communicator", dev);
+    }
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclComm_t c = nullptr;
+    RT_CHECK(cudaSetDevice(dev));
+    NCCL_CHECK(g_nccl.CommInitRank(&c, nranks, uid, rank));
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_dev[dev].comm = c;
+    return 0;
+}
+
+int mt_nccl_destroy(int dev) {
+    ncclComm_t c = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (dev < 0 || dev >= kMaxDev) return fail("device index %d out of range", dev);
+        c = g_dev[dev].comm;
+        g_dev[dev].comm = nullptr;
+    }
+    if (c) NCCL_CHECK(g_nccl.CommDestroy(c));
+    return 0;
+}
+
+int mt_allreduce_f64(int dev, uint64_t buf, uint64_t count, int op, uint64_t out_f32) {
+    static const ncclRedOp_t kOps[4] = {ncclSum, ncclMax, ncclMin, ncclProd};
+    if (op < 0 || op > 3) return fail("mt_allreduce_f64: op %d is not 0..3", op);
+    Buffer b, o{};
+    cudaStream_t st;
+    ncclComm_t c;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (ensure_dev(dev)) return 1;
+        if (get_buf(buf, &b)) return 1;
+        if (out_f32 && get_buf(out_f32, &o)) return 1;
+        st = g_dev[dev].stream;
+        c = g_dev[dev].comm;
+    }
+    if (!c) return fail("mt_allreduce_f64: device %d has no communicator (mt_nccl_init)", dev);
+    if (b.dev != dev || count * sizeof(double) > b.size) return fail("mt_allreduce_f64: buffer too small or on another device");
+    if (out_f32 && (o.dev != dev || count * sizeof(float) > o.size))
+        return fail("mt_allreduce_f64: output buffer too small or on another device");
+    RT_CHECK(cudaSetDevice(dev));
+    NCCL_CHECK(g_nccl.AllReduce(b.ptr, b.ptr, count, ncclFloat64, kOps[op], c, st));
+    if (out_f32) {
+        const unsigned threads = 256;
+        const unsigned blocks = (unsigned)((count + threads - 1) / threads);
+        f64_to_f32<<<blocks, threads, 0, st>>>((const double*)b.ptr, (float*)o.ptr, count);
+        RT_CHECK(cudaGetLastError());
+    }
+    return 0;
 }
 
 int mt_sync(int dev) {

@@ -31,12 +31,24 @@ def assemble_split_reduction(decision: DecisionView, function_name: str | None) 
     case): the native split-row kernel of the backend (``mt_reduce_rows``), fp64
     partials combined deterministically. The reference runs such a reduction on a
     single threadgroup (assembly/reduction.py:105-106)."""
+    from metellus_b200 import distributed
+
     anchor = decision.anchor
+    combine = anchor.out.name in distributed.combined_outputs()
     if decision.strategy is not FusionStrategy.STANDALONE_REDUCTION or len(anchor.input.shape) != 2:
+        if combine:
+            raise ValueError(f"reduction {anchor.out.name!r} is combined across GPUs, so it must be a standalone "
+                             "2-D reduction (no fused prologue / epilogue)")
         return None
     src = anchor.input
     M, K = src.shape
-    if M > SPLIT_MAX_ROWS or K < SPLIT_MIN_COLS or src.col_stride != 1 or (M > 1 and src.row_stride < K):
+    layout_ok = src.col_stride == 1 and (M == 1 or src.row_stride >= K)
+    if combine:
+        if not layout_ok or M > SPLIT_MAX_ROWS:
+            raise ValueError(f"reduction {anchor.out.name!r} is combined across GPUs but its input is not a "
+                             f"row-major matrix of at most {SPLIT_MAX_ROWS} rows")
+        return _combined_reduction(decision, function_name, src, M, K)
+    if M > SPLIT_MAX_ROWS or K < SPLIT_MIN_COLS or not layout_ok:
         return None
     ld = src.row_stride if M > 1 else K
     ctx = CodegenContext(function_name=function_name or f"reduce_split_{anchor.out.name}",
@@ -46,6 +58,24 @@ def assemble_split_reduction(decision: DecisionView, function_name: str | None) 
     return KernelGroup(kernel=kernel, bindings=(src.buffer_key, anchor.out.buffer_key), dims=(M, K),
                        grid=(0, M, 1), threads=(256, 1, 1), ops=decision.ops, strategy=decision.strategy,
                        pipe="native")
+
+
+PARTIAL_KEY = "__mt_partial64"
+
+
+def _combined_reduction(decision: DecisionView, function_name: str | None, src, M: int, K: int) -> KernelGroup:
+    """Sharded whole-tensor reduction: this rank's fp64 partials (``mt_reduce_rows``
+    with fp64 output, into scratch), then one NCCL all-reduce of the partials across
+    the ranks that also writes the fp32 result (``mt_allreduce_f64``)."""
+    anchor = decision.anchor
+    ld = src.row_stride if M > 1 else K
+    ctx = CodegenContext(function_name=function_name or f"reduce_allreduce_{anchor.out.name}",
+                         buffers=(param_decl(src.buffer_key), param_decl(anchor.out.buffer_key, writable=True)),
+                         dims=("M", "K"), tg_x=256, tg_y=1)
+    kernel = NativeKernel("mt_reduce_rows+mt_allreduce_f64", (M, K, ld, anchor.op), ctx)
+    return KernelGroup(kernel=kernel, bindings=(src.buffer_key, anchor.out.buffer_key), dims=(M, K),
+                       grid=(0, M, 1), threads=(256, 1, 1), ops=decision.ops, strategy=decision.strategy,
+                       pipe="native+nccl", scratch=((PARTIAL_KEY, 8 * M),))
 
 
 def assemble_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup:

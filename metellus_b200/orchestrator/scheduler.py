@@ -18,7 +18,7 @@ import numpy as np
 
 from metellus_b200.orchestrator.builder import Operations
 from metellus_b200.orchestrator.dag import build_dag
-from metellus_b200.orchestrator.kernel_group import KernelGroup
+from metellus_b200.orchestrator.kernel_group import STATUS_KEY, KernelGroup
 from metellus_b200.runtime.program import (
     Allocate,
     CheckStatus,
@@ -129,6 +129,7 @@ def schedule(ops: Operations, groups: tuple[KernelGroup, ...], *, profile: bool 
                 steps.append(Free(name=k))
             freed.add(k)
     for k in scratch:
-        steps.append(CheckStatus(name=k))
+        if k == STATUS_KEY:
+            steps.append(CheckStatus(name=k))
         steps.append(Free(name=k))
     return Runtime(tuple(steps))

@@ -58,7 +58,7 @@ EXPORTED = (
     "mt_host_free", "mt_nvrtc_compile", "mt_kernel_load", "mt_kernel_info", "mt_launch", "mt_sync",
     "mt_event_create", "mt_event_record", "mt_event_elapsed", "mt_event_destroy",
     "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy", "mt_reduce_rows",
-    "mt_reduce_rows_noalloc",
+    "mt_reduce_rows_noalloc", "mt_nccl_unique_id", "mt_nccl_init", "mt_nccl_destroy", "mt_allreduce_f64",
 )
 
 
@@ -112,6 +112,10 @@ def lib() -> ctypes.CDLL:
                 "mt_reduce_rows": [i32, u64, u64, u64, u64, u64, i32, P(ctypes.c_float)],
                 "mt_reduce_rows_noalloc": [i32, ctypes.c_void_p, ctypes.c_void_p, u64, u64, u64, i32,
                                            ctypes.c_void_p],
+                "mt_nccl_unique_id": [ctypes.c_char_p, u64],
+                "mt_nccl_init": [i32, i32, i32, ctypes.c_char_p],
+                "mt_nccl_destroy": [i32],
+                "mt_allreduce_f64": [i32, u64, u64, i32, u64],
             }
             for name, args in sig.items():
                 fn = getattr(L, name)
@@ -327,15 +331,46 @@ def run_kernel(source: str, function_name: str, buffers, grid, threads, *, dims=
 
 
 REDUCE_OPS = {"sum": 0, "max": 1, "min": 2, "product": 3}
+# fp64-output forms (a per-GPU partial of a sharded reduction)
+REDUCE_OPS_F64 = {k: v + 4 for k, v in REDUCE_OPS.items()}
 
 
 def reduce_rows(in_handle: int, out_handle: int, rows: int, cols: int, ld: int, op: str, *,
                 timed: bool = False, dev: int | None = None) -> float | None:
-    """Native split-row reduction (``mt_reduce_rows``): out[r] = op(in[r, :])."""
+    """Native split-row reduction (``mt_reduce_rows``): out[r] = op(in[r, :]); an op
+    name ending in ``_f64`` writes fp64 results."""
     ms = ctypes.c_float(0.0)
+    code = REDUCE_OPS_F64[op[:-4]] if op.endswith("_f64") else REDUCE_OPS[op]
     _check(lib().mt_reduce_rows(_device if dev is None else dev, in_handle, out_handle, rows, cols, ld,
-                                REDUCE_OPS[op], ctypes.byref(ms) if timed else None))
+                                code, ctypes.byref(ms) if timed else None))
     return float(ms.value) if timed else None
+
+
+# -- NCCL ------------------------------------------------------------------------------
+
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    _check(lib().mt_nccl_unique_id(buf, NCCL_ID_BYTES))
+    return buf.raw
+
+
+def nccl_init(nranks: int, rank: int, uid: bytes, dev: int | None = None) -> None:
+    if len(uid) != NCCL_ID_BYTES:
+        raise ValueError(f"NCCL id must be {NCCL_ID_BYTES} bytes, got {len(uid)}")
+    _check(lib().mt_nccl_init(_device if dev is None else dev, nranks, rank, uid))
+
+
+def nccl_destroy(dev: int | None = None) -> None:
+    _check(lib().mt_nccl_destroy(_device if dev is None else dev))
+
+
+def allreduce_f64(buf_handle: int, count: int, op: str = "sum", out_f32: int = 0, dev: int | None = None) -> None:
+    """In-place NCCL all-reduce of ``count`` doubles (stream ordered); optionally
+    also writes the fp32-rounded result into ``out_f32``."""
+    _check(lib().mt_allreduce_f64(_device if dev is None else dev, buf_handle, count, REDUCE_OPS[op], out_f32))
 
 
 # -- events / graphs -------------------------------------------------------------------

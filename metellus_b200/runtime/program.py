@@ -228,6 +228,20 @@ class NativeKernel(Kernel):
         if self.entry == "mt_reduce_rows":
             rows, cols, ld, op = self.params
             return backend.reduce_rows(handles[0], handles[1], rows, cols, ld, op, timed=timed)
+        if self.entry == "mt_reduce_rows+mt_allreduce_f64":
+            # handles: input, output, fp64 partial scratch
+            rows, cols, ld, op = self.params
+            t0 = backend.Event() if timed else None
+            if t0 is not None:
+                t0.record()
+            backend.reduce_rows(handles[0], handles[2], rows, cols, ld, op + "_f64")
+            backend.allreduce_f64(handles[2], rows, op, out_f32=handles[1])
+            if t0 is None:
+                return None
+            t1 = backend.Event()
+            t1.record()
+            backend.sync()
+            return t0.elapsed_ms(t1)
         raise ValueError(f"unknown native kernel {self.entry!r}")
 
 
