@@ -413,40 +413,35 @@ def committed_traffic(key: str, g) -> float | None:
 
 
 def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
-    """Same program through the public path with host buffers: pinned host inputs
-    copied in, all kernels, the output copied back — all inside CUDA events."""
-    from metellus_b200.orchestrator.scheduler import buffer_sizes, dispatch_of
+    """Same program through the public API with host buffers: ``Executable`` (compiled
+    once, persistent device buffers, kernels replayed from a CUDA graph) called on
+    pinned host inputs, writing the output into a pinned host array; each step's
+    host-to-device input copies, kernels and device-to-host output copy are inside the
+    CUDA events."""
+    from metellus_b200 import distributed
+    from metellus_b200.api.executable import Executable
     from metellus_b200.runtime import backend
-    from metellus_b200.runtime.buffer import Buffer
 
-    tensors = ops.tensors
-    uploads = ops.uploads
+    out_name = configs.CONFIGS[key].output
+    combine = (out_name,) if key == "c3sum" and world > 1 else ()
+    with distributed.combining(*combine):
+        exe = Executable(ops, outputs=(out_name,))
     pinned = {}
-    for n, a in uploads.items():
+    for n, a in ops.uploads.items():
         pa = backend.PinnedArray(a.shape)
         pa.array[...] = a
-        pinned[tensors[n].buffer_key] = pa
-    out_name = configs.CONFIGS[key].output
-    out_t = tensors[out_name]
-    out_host = backend.PinnedArray(out_t.shape)
-    sizes = buffer_sizes(ops, groups)
-    env = {}
-    dispatches = [dispatch_of(g) for g in groups]
-    for d in dispatches:
-        for k in d.bindings:
-            if k not in env:
-                env[k] = Buffer.zeros(sizes[k])
+        pinned[n] = pa
+    out_host = backend.PinnedArray(ops.tensors[out_name].shape)
+    inputs = {n: p.array for n, p in pinned.items()}
+    outs = {out_name: out_host.array}
 
     def step():
-        for k, pa in pinned.items():
-            env[k].write(pa.array, wait=False)
-        for d in dispatches:
-            d.execute(env)
-        env[out_t.buffer_key].read_into(out_host.array, wait=False)
+        exe(inputs, out=outs, wait=False)
 
     steps = max(3, min(args.steps, 10))
     for _ in range(3):
         step()
+    exe.synchronize()
     barrier()
     e0, e1 = backend.Event(), backend.Event()
     e0.record()
@@ -454,6 +449,7 @@ def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
         step()
     e1.record()
     barrier()
+    exe.synchronize()
     ms = e0.elapsed_ms(e1) / steps
     if dist is not None:
         import torch
@@ -463,9 +459,10 @@ def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
         ms = float(t.item())
     h2d = int(sum(p.array.nbytes for p in pinned.values()))
     d2h = int(out_host.array.nbytes)
+    exe.close()
     _, unit, _ = metric_of(key)
     return {"value": amount(key, shape) * world / (ms / 1e3), "unit": unit, "ms_per_step": ms,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": "metellus_b200.Executable"}
 
 
 if __name__ == "__main__":

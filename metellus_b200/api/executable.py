@@ -1,0 +1,136 @@
+"""A program compiled once and bound to device memory for repeated execution.
+
+``run(ops)`` (reference: src/api/run.py) plans, compiles, allocates, runs and frees on
+every call, like the reference. Serving loops and benchmarks call the same program
+many times on new inputs; ``Executable`` does the planning and compilation once,
+keeps every bound device buffer for its lifetime (a persistent pool for the
+program), and replays the dispatch list from a CUDA graph (captured on the second
+call, after the first call has loaded every module), so a call costs the input
+copies, one graph launch and the output copies::
+
+    exe = Executable(ops, outputs=("out",))
+    res = exe({"x": x, "y": y, "z": z})          # dict name -> host ndarray
+    exe(inputs, out={"out": pinned}, wait=False)  # asynchronous with pinned buffers
+
+Inputs are the program's ``from_numpy`` / ``input`` tensors by name; host arrays in
+page-locked memory (``backend.PinnedArray``) copy asynchronously.
+"""
+
+from __future__ import annotations
+
+from typing import Iterable
+
+import numpy as np
+
+from metellus_b200.api.run import compile_program
+from metellus_b200.orchestrator.builder import Operations
+from metellus_b200.orchestrator.kernel_group import STATUS_KEY
+from metellus_b200.orchestrator.scheduler import buffer_sizes, dispatch_of, scratch_of
+from metellus_b200.runtime import backend
+from metellus_b200.runtime.buffer import Buffer
+from metellus_b200.runtime.program import CheckStatus
+
+
+class Executable:
+    def __init__(self, ops: Operations, outputs: Iterable[str] | None = None, *, graph: bool = True,
+                 b200: bool = True) -> None:
+        self.ops = ops
+        self.groups = compile_program(ops, b200=b200)
+        tensors = ops.tensors
+        program = ops.build()
+        produced = {op.out.name for op in program}
+        used = {t.name for op in program for t in op.inputs}
+        self.outputs = tuple(outputs) if outputs is not None else tuple(sorted(produced - used))
+        bound = {k for g in self.groups for k in g.bindings}
+        for name in self.outputs:
+            if name not in tensors:
+                raise KeyError(f"Executable: unknown output {name!r}")
+            if tensors[name].buffer_key not in bound:
+                raise ValueError(f"Executable: {name!r} is fused away (not materialised by the plan)")
+        self.input_keys = {name: tensors[name].buffer_key for name in ops.uploads}
+        sizes = buffer_sizes(ops, self.groups)
+        self.env: dict[str, Buffer] = {}
+        for name, arr in ops.uploads.items():
+            self.env[tensors[name].buffer_key] = Buffer.from_numpy(arr)
+        for k, n in scratch_of(self.groups).items():
+            self.env[k] = Buffer.zeros(n)
+        for g in self.groups:
+            for k in g.bindings:
+                if k not in self.env:
+                    self.env[k] = Buffer(sizes[k])
+        self.dispatches = tuple(dispatch_of(g) for g in self.groups)
+        for g in self.groups:
+            _ = g.kernel.handle  # compile + load before the first call
+        # collectives and the host-timed paths stay out of graphs
+        self._graph_ok = graph and not any("nccl" in (g.pipe or "") for g in self.groups)
+        self._graph: int | None = None
+        self._calls = 0
+
+    # -- execution ------------------------------------------------------------------
+
+    def _launch(self) -> None:
+        if self._graph is not None:
+            backend.graph_launch(self._graph)
+            return
+        if self._graph_ok and self._calls >= 1:
+            backend.graph_begin()
+            try:
+                for d in self.dispatches:
+                    d.execute(self.env)
+            except Exception:
+                try:
+                    backend.graph_end()
+                except Exception:
+                    pass
+                self._graph_ok = False
+                raise
+            self._graph = backend.graph_end()
+            backend.graph_launch(self._graph)
+            return
+        for d in self.dispatches:
+            d.execute(self.env)
+
+    def __call__(self, inputs: dict[str, np.ndarray] | None = None, out: dict[str, np.ndarray] | None = None, *,
+                 wait: bool = True) -> dict[str, np.ndarray]:
+        tensors = self.ops.tensors
+        for name, arr in (inputs or {}).items():
+            if name not in self.input_keys:
+                raise KeyError(f"Executable: {name!r} is not an input of the program")
+            if tuple(np.shape(arr)) != tuple(tensors[name].shape):
+                raise ValueError(f"Executable: input {name!r} has shape {np.shape(arr)}, "
+                                 f"expected {tensors[name].shape}")
+            self.env[self.input_keys[name]].write(np.asarray(arr, dtype=np.float32), wait=False)
+        self._launch()
+        self._calls += 1
+        results: dict[str, np.ndarray] = {}
+        for name in self.outputs:
+            t = tensors[name]
+            dst = (out or {}).get(name)
+            if dst is None:
+                dst = np.empty(t.shape, dtype=np.float32)
+            if t.buffer_key != t.name:
+                raise ValueError(f"Executable: output {name!r} is a view; request its owner {t.buffer_key!r}")
+            results[name] = self.env[t.buffer_key].read_into(dst, wait=False)
+        if wait:
+            self.synchronize()
+        return results
+
+    def synchronize(self) -> None:
+        """Wait for the device, then raise if a kernel's bounded wait timed out."""
+        backend.sync()
+        if STATUS_KEY in self.env:
+            CheckStatus(STATUS_KEY).execute(self.env)
+
+    def close(self) -> None:
+        if self._graph is not None:
+            backend.graph_destroy(self._graph)
+            self._graph = None
+        for b in self.env.values():
+            b.release()
+        self.env.clear()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
