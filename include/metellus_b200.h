@@ -53,6 +53,8 @@ int mt_buffer_write_async(uint64_t handle, const void* src, size_t nbytes);
 int mt_buffer_read_async(uint64_t handle, void* dst, size_t nbytes);
 /* Set every byte to `value`. */
 int mt_buffer_fill(uint64_t handle, uint8_t value);
+/* Stream-ordered form of mt_buffer_fill: returns without waiting for the device. */
+int mt_buffer_fill_async(uint64_t handle, uint8_t value);
 /* Pinned host memory for fast host<->device copies. */
 int mt_host_alloc(size_t nbytes, void** ptr);
 int mt_host_free(void* ptr);

@@ -407,6 +407,19 @@ int mt_buffer_fill(uint64_t handle, uint8_t value) {
     return 0;
 }
 
+int mt_buffer_fill_async(uint64_t handle, uint8_t value) {
+    Buffer b;
+    cudaStream_t s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (get_buf(handle, &b)) return 1;
+        s = g_dev[b.dev].stream;
+    }
+    RT_CHECK(cudaSetDevice(b.dev));
+    RT_CHECK(cudaMemsetAsync(b.ptr, value, b.size, s));
+    return 0;
+}
+
 int mt_host_alloc(size_t nbytes, void** ptr) {
     RT_CHECK(cudaHostAlloc(ptr, nbytes, cudaHostAllocPortable));
     return 0;

@@ -54,7 +54,7 @@ class MtTmapSpec(ctypes.Structure):
 EXPORTED = (
     "mt_last_error", "mt_device_count", "mt_init", "mt_device_attr", "mt_buffer_create",
     "mt_buffer_release", "mt_buffer_size", "mt_buffer_ptr", "mt_buffer_write", "mt_buffer_read",
-    "mt_buffer_write_async", "mt_buffer_read_async", "mt_buffer_fill", "mt_host_alloc",
+    "mt_buffer_write_async", "mt_buffer_read_async", "mt_buffer_fill", "mt_buffer_fill_async", "mt_host_alloc",
     "mt_host_free", "mt_nvrtc_compile", "mt_kernel_load", "mt_kernel_info", "mt_launch", "mt_sync",
     "mt_event_create", "mt_event_record", "mt_event_elapsed", "mt_event_destroy",
     "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy", "mt_reduce_rows",
@@ -91,6 +91,7 @@ def lib() -> ctypes.CDLL:
                 "mt_buffer_write_async": [u64, ctypes.c_void_p, sz],
                 "mt_buffer_read_async": [u64, ctypes.c_void_p, sz],
                 "mt_buffer_fill": [u64, ctypes.c_uint8],
+                "mt_buffer_fill_async": [u64, ctypes.c_uint8],
                 "mt_host_alloc": [sz, P(ctypes.c_void_p)],
                 "mt_host_free": [ctypes.c_void_p],
                 "mt_nvrtc_compile": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_void_p, sz,
@@ -207,8 +208,8 @@ def read_buffer(handle: int, out: np.ndarray, *, wait: bool = True) -> None:
     _check(fn(handle, out.ctypes.data, out.nbytes))
 
 
-def fill_buffer(handle: int, value: int) -> None:
-    _check(lib().mt_buffer_fill(handle, value))
+def fill_buffer(handle: int, value: int, *, wait: bool = True) -> None:
+    _check((lib().mt_buffer_fill if wait else lib().mt_buffer_fill_async)(handle, value))
 
 
 class PinnedArray:
@@ -317,6 +318,36 @@ def launch(
     _check(lib().mt_launch(_device if dev is None else dev, kernel, bufs, nb, dims_arr, nd, g, b, int(smem),
                            int(cluster_x), specs, nt, ctypes.byref(ms) if timed else None))
     return float(ms.value) if timed else None
+
+
+class PreparedLaunch:
+    """The ctypes argument block of one launch, built once and reused: a dispatch
+    replayed many times on the same buffers pays only the ``mt_launch`` call."""
+
+    __slots__ = ("kernel", "bufs", "nb", "dims", "nd", "grid", "block", "smem", "cluster_x", "specs", "nt", "dev")
+
+    def __init__(self, kernel: int, buffers, dims, grid, threads, *, smem: int = 0, cluster_x: int = 1,
+                 tmaps: tuple = (), dev: int | None = None) -> None:
+        self.kernel = kernel
+        self.nb = len(buffers)
+        self.bufs = (ctypes.c_uint64 * max(self.nb, 1))(*buffers)
+        self.nd = len(dims)
+        self.dims = (ctypes.c_uint32 * max(self.nd, 1))(*[int(d) & 0xFFFFFFFF for d in dims])
+        self.grid = (ctypes.c_uint32 * 3)(*grid)
+        self.block = (ctypes.c_uint32 * 3)(*threads)
+        self.smem = int(smem)
+        self.cluster_x = int(cluster_x)
+        self.nt = len(tmaps)
+        self.specs = (MtTmapSpec * max(self.nt, 1))()
+        for i, t in enumerate(tmaps):
+            self.specs[i] = t.to_ctypes()
+        self.dev = _device if dev is None else dev
+
+    def __call__(self, timed: bool = False) -> float | None:
+        ms = ctypes.c_float(0.0)
+        _check(lib().mt_launch(self.dev, self.kernel, self.bufs, self.nb, self.dims, self.nd, self.grid, self.block,
+                               self.smem, self.cluster_x, self.specs, self.nt, ctypes.byref(ms) if timed else None))
+        return float(ms.value) if timed else None
 
 
 def run_kernel(source: str, function_name: str, buffers, grid, threads, *, dims=(), smem: int = 0,

@@ -264,15 +264,20 @@ class Dispatch:
                 f"Dispatch: expected {len(self.kernel.dim_names)} dim values "
                 f"({self.kernel.dim_names}), got {len(self.dims)}"
             )
-        handles = [env[name].handle for name in self.bindings]
+        handles = tuple(env[name].handle for name in self.bindings)
         if isinstance(self.kernel, NativeKernel):
-            t = self.kernel.launch(handles, self.time_key is not None)
+            t = self.kernel.launch(list(handles), self.time_key is not None)
             if self.time_key is not None:
                 env[self.time_key] = float(t)
             return
-        t = backend.launch(self.kernel.handle, handles, self.dims, self.grid, self.threads,
-                           smem=self.kernel.smem_bytes, tmaps=self.tmaps, cluster_x=self.cluster_x,
-                           timed=self.time_key is not None)
+        # the argument block is rebuilt only when the bound buffers change
+        cached = self.__dict__.get("_prepared")
+        if cached is None or cached[0] != (handles, backend.current_device()):
+            prep = backend.PreparedLaunch(self.kernel.handle, handles, self.dims, self.grid, self.threads,
+                                          smem=self.kernel.smem_bytes, tmaps=self.tmaps, cluster_x=self.cluster_x)
+            cached = ((handles, backend.current_device()), prep)
+            object.__setattr__(self, "_prepared", cached)
+        t = cached[1](timed=self.time_key is not None)
         if self.time_key is not None:
             env[self.time_key] = float(t)
 
