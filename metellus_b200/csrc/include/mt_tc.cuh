@@ -441,6 +441,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     constexpr uint32_t NCOLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
     static_assert(TCOLS <= 512, "accumulators and A stages exceed TMEM");
     static_assert(BN == 64 || BN == 128, "BN must be 64 or 128");
+    static_assert(NB * BN <= 256, "one MMA covers every anchor: N = NB * BN <= 256");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
     constexpr int NCONV = 6;
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -454,13 +455,32 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
-    const int m0 = (int)blockIdx.y * 128, n0 = (int)blockIdx.x * BN;
+    // Tile order: the launch is (N tiles, M tiles); CTAs are mapped so that the ~148
+    // resident at a time cover groups of 8 M tiles x ~18 N tiles, so each A row block
+    // and each B column block is fetched from DRAM about once per group instead of
+    // once per M tile (row-major order streams all of B once per M tile when B does
+    // not fit L2).
+    int m0, n0;
+    {
+        constexpr int kGroupM = 8;
+        const int n_tiles = (int)gridDim.x, m_tiles = (int)gridDim.y;
+        const int id = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+        const int group = id / (kGroupM * n_tiles);
+        const int first_m = group * kGroupM;
+        const int gsize = min(m_tiles - first_m, kGroupM);
+        const int in_group = id - group * kGroupM * n_tiles;
+        m0 = (first_m + in_group % gsize) * 128;
+        n0 = (in_group / gsize) * BN;
+    }
     const int nk = (K + 31) / 32;
     const int nchunks = (nk + CHUNK - 1) / CHUNK;
     auto A_raw = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
+    // B tiles of all anchors side by side (hi: anchor 0, anchor 1; then lo likewise),
+    // so one MMA with N = NB * BN covers every anchor: anchor b's columns land at
+    // accumulator columns [b * BN, (b + 1) * BN).
     auto B_slot = [&](int s, int b, int j) {
         return reinterpret_cast<float*>(smem + s * L::kStageBytes + L::kABytes +
-                                        (b * L::kBSlots + j) * L::kBBytes);
+                                        (j * NB + b) * L::kBBytes);
     };
     auto B_dst = [&](int s, int b) { return B_slot(s, b, 0); };
     auto B_hi = [&](int s, int b) { return B_slot(s, b, 0); };
@@ -513,7 +533,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = mt_idesc_tf32(128, BN, false, B_MN);
+            constexpr uint32_t idesc = mt_idesc_tf32(128, NB * BN, false, B_MN);
             bool ok = true;
             for (int c = 0; c < nchunks && ok; ++c) {
                 const int tb = c & 1;
@@ -532,17 +552,14 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t dah = ah + 8u * (uint32_t)kk;
                         const uint32_t dal = dah + 32u;
-#pragma unroll
-                        for (int b = 0; b < NB; ++b) {
-                            const uint32_t d = tmem + (uint32_t)((tb * NB + b) * BN);
-                            const uint64_t dbh = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_hi(s, b)), kk)
-                                                      : mt_operand_desc_k(mt_smem_u32(B_hi(s, b)), kk);
-                            const uint64_t dbl = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_lo(s, b)), kk)
-                                                      : mt_operand_desc_k(mt_smem_u32(B_lo(s, b)), kk);
-                            mt_mma_tf32_ts(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
-                            mt_mma_tf32_ts(d, dal, dbh, idesc, 1u);
-                            mt_mma_tf32_ts(d, dah, dbh, idesc, 1u);
-                        }
+                        const uint32_t d = tmem + (uint32_t)(tb * NB * BN);
+                        const uint64_t dbh = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_hi(s, 0)), kk)
+                                                  : mt_operand_desc_k(mt_smem_u32(B_hi(s, 0)), kk);
+                        const uint64_t dbl = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_lo(s, 0)), kk)
+                                                  : mt_operand_desc_k(mt_smem_u32(B_lo(s, 0)), kk);
+                        mt_mma_tf32_ts(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
+                        mt_mma_tf32_ts(d, dal, dbh, idesc, 1u);
+                        mt_mma_tf32_ts(d, dah, dbh, idesc, 1u);
                     }
                     mt_mma_commit(&empty[s]);
                 }
