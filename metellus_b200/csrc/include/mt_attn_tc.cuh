@@ -11,26 +11,34 @@
 // output rows in registers (O = O * alpha + P_i V_i), so the tensor core's own fp32
 // accumulation never runs longer than one 64-key block.
 //
+// Pipelining: S and the P V products are double buffered, P single buffered. The
+// softmax of block i computes its exponentials while P V of block i - 1 and Q K of
+// block i + 1 run; it waits for P V of block i - 1 only to overwrite P, writes P_i,
+// and then folds P V of block i - 1 into the output (off the P -> P V critical path,
+// while P V of block i and Q K of block i + 2 run). Shared memory carries only the K / V
+// tiles: Q and P, the A operands, live in tensor memory.
+//
 // 512 threads, 16 warps:
 //   warp 0       TMA producer: Q once, then K_i / V_i into a 2-stage ring
 //   warp 1       TMEM owner + MMA issuer (QK_0, QK_1, then PV_i, QK_{i+2} per block)
 //   warps 2..7   converters: split K_i and V_i into hi / lo in place
 //   warps 8..15  softmax + output: thread = (query row = TMEM lane, half h of the
 //                block's 64 keys and of the 64 output features); warp 8+q and 12+q
-//                share lane quarter q. Per block: read its 32 scores, exchange the
-//                half-row max with its partner thread (smem + mbarrier), exponentiate,
-//                fold the previous block's P V into its 32 output registers
-//                (O = O * alpha + P V), write its P hi / lo to tensor memory.
+//                share lane quarter q. Warps 8..11 first split Q (row = lane) into
+//                TMEM. Per block: read its 32 scores, exchange the half-row max with its
+//                partner thread (smem + mbarrier), exponentiate, write its P hi / lo to
+//                tensor memory, fold the previous block's P V into its 32 output
+//                registers.
 //
 // Tensor memory (512 columns): Q hi/lo [0,128), S buffers [128,192) [192,256),
-// P hi/lo [256,384), P V [384,448).
+// P hi/lo [256,384), P V buffers [384,448) [448,512).
 //
 // Every wait is bounded (mt_mbar_wait); on a timeout the status word is set, every
 // role leaves its loop, in-flight copies and MMAs are drained and the kernel returns.
 #pragma once
 
 struct mt_fa_layout {
-    static constexpr uint32_t kQ = 0;                        // Q raw: 2 k-tiles x 16 KB (128 rows x 128 B)
+    static constexpr uint32_t kQ = 0;                        // Q (TMA target): 2 k-tiles x 16 KB
     static constexpr uint32_t kStage0 = 32768;               // per stage: K hi, K lo, V hi, V lo (16 KB each)
     static constexpr uint32_t kStageBytes = 4u * 16384u;
     static constexpr uint32_t kXch = kStage0 + 2u * kStageBytes;    // float x[2 parity][2 half][128]
@@ -70,7 +78,7 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
     const int q0 = (int)blockIdx.x * 128, bz = (int)blockIdx.z;
     const int nb = Sk / 64;
-    auto Qraw = [&](int j) { return reinterpret_cast<float*>(smem + L::kQ + j * 16384); };
+    auto Qs = [&](int j) { return reinterpret_cast<float*>(smem + L::kQ + j * 16384); };
     auto Khi = [&](int s) { return reinterpret_cast<float*>(smem + L::kStage0 + s * L::kStageBytes); };
     auto Klo = [&](int s) { return reinterpret_cast<float*>(smem + L::kStage0 + s * L::kStageBytes + 16384); };
     auto Vhi = [&](int s) { return reinterpret_cast<float*>(smem + L::kStage0 + s * L::kStageBytes + 32768); };
@@ -78,7 +86,7 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
 
     if (threadIdx.x == 0) {
         // arrival counts: 1 = TMA expect_tx / tcgen05.commit, 4 = one lane per Q
-        // converting warp, 6 = one lane per converter warp, 8 = one lane per softmax
+        // splitting warp, 6 = one lane per converter warp, 8 = one lane per softmax
         // warp, 64 = every thread of a softmax warp pair
         for (int i = 0; i < 29; ++i) {
             const uint32_t n = i == 1 ? 4u : (i >= 6 && i <= 9) ? 6u : (i >= 16 && i <= 18) ? 8u
@@ -102,8 +110,8 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
     if (warp == 0) {
         if (lane == 0) {
             mt_mbar_expect_tx(qfull, 32768);
-            mt_tma_load_3d(Qraw(0), tmQ, qfull, 0, q0, bz);
-            mt_tma_load_3d(Qraw(1), tmQ, qfull, 32, q0, bz);
+            mt_tma_load_3d(Qs(0), tmQ, qfull, 0, q0, bz);
+            mt_tma_load_3d(Qs(1), tmQ, qfull, 32, q0, bz);
             int kiss = 0, viss = 0;
             for (int i = 0; i < nb; ++i) {
                 const int s = i & 1;
@@ -157,11 +165,12 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
             if (ok && nb > 1) ok = issue_qk(1);
             for (int i = 0; i < nb && ok; ++i) {
                 const int s = i & 1;
-                // pfull(i) also means the softmax threads have read P V of block i - 1
+                // pfull(i) also means the softmax threads have folded P V of block i - 2
+                // out of this block's P V buffer
                 if (!mt_mbar_wait(pfull, (uint32_t)i & 1u, abort_flag, status, 2)) break;
                 if (!mt_mbar_wait(&vconv[s], (uint32_t)(i >> 1) & 1u, abort_flag, status, 2)) break;
                 mt_tc_fence_after();
-                const uint32_t d = tmem + OC;
+                const uint32_t d = tmem + OC + 64u * (uint32_t)s;
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     const uint32_t vh = mt_smem_u32(Vhi(s) + j * 2048), vl = mt_smem_u32(Vlo(s) + j * 2048);
@@ -202,14 +211,17 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
     } else {
         const int q = warp & 3, h = (warp - 8) >> 2, r = q * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-        bool ok = mt_mbar_wait(qfull, 0, abort_flag, status, 4);
-        if (ok && h == 0) {
-            const mt_no_prologue np{};
-            mt_convert_a_rows(Qraw(0), tmem + QC, q, lane, 0, 0, 0, 0, np);
-            mt_convert_a_rows(Qraw(1), tmem + QC + 64u, q, lane, 0, 0, 0, 0, np);
-            mt_tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mt_mbar_arrive(qconv);
+        bool ok = true;
+        if (h == 0) {
+            ok = mt_mbar_wait(qfull, 0, abort_flag, status, 4);
+            if (ok) {
+                const mt_no_prologue np{};
+                mt_convert_a_rows(Qs(0), tmem + QC, q, lane, 0, 0, 0, 0, np);
+                mt_convert_a_rows(Qs(1), tmem + QC + 64u, q, lane, 0, 0, 0, 0, np);
+                mt_tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mt_mbar_arrive(qconv);
+            }
         }
         // half-row exchange with the partner thread (same row, other half)
         auto exchange = [&](int blk, float v) -> float {
@@ -225,7 +237,20 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
         float o[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) o[j] = 0.0f;
-        float m = -INFINITY, l = 0.0f, a_prev = 0.0f;
+        // fold P V of block `blk` (finished: its pempty waited) into the output registers
+        auto fold = [&](int blk, float alpha) {
+            mt_tc_fence_after();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                float t[16];
+                mt_tmem_ld16(tmem + lane_off + OC + 64u * (uint32_t)(blk & 1) + 32u * (uint32_t)h +
+                                 16u * (uint32_t)hh, t);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[16 * hh + j] = fmaf(o[16 * hh + j], alpha, t[j]);
+            }
+        };
+        float m = -INFINITY, l = 0.0f;
+        float a_prev = 0.0f;  // alpha of the previous block
         for (int i = 0; i < nb && ok; ++i) {
             const int s = i & 1;
             if (!mt_mbar_wait(&sfull[s], (uint32_t)(i >> 1) & 1u, abort_flag, status, 4)) {
@@ -261,22 +286,13 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
             }
             l = fmaf(l, alpha, __fadd_rn(__fadd_rn(ps[0], ps[1]), __fadd_rn(ps[2], ps[3])));
             m = mn;
-            // P V of block i - 1 is done: fold it into the output, then P is free
-            if (i >= 1) {
-                if (!mt_mbar_wait(pempty, (uint32_t)(i - 1) & 1u, abort_flag, status, 4)) {
-                    ok = false;
-                    break;
-                }
-                mt_tc_fence_after();
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    float t[16];
-                    mt_tmem_ld16(tmem + lane_off + OC + 32u * (uint32_t)h + 16u * (uint32_t)hh, t);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) o[16 * hh + j] = fmaf(o[16 * hh + j], a_prev, t[j]);
-                }
+            // P V of block i - 1 done: P is free (its product is folded below)
+            if (i >= 1 && !mt_mbar_wait(pempty, (uint32_t)(i - 1) & 1u, abort_flag, status, 4)) {
+                ok = false;
+                break;
             }
-            a_prev = alpha;
+            mt_tc_fence_after();
+            const uint32_t pbuf = tmem + lane_off + PC + 64u * (uint32_t)h;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
                 float lo[16];
@@ -285,22 +301,20 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
                     const float x = sv[16 * hh + k];
                     mt_split_tf32(x, sv[16 * hh + k], lo[k]);
                 }
-                mt_tmem_st16(tmem + lane_off + PC + 64u * (uint32_t)h + 16u * (uint32_t)hh, &sv[16 * hh]);
-                mt_tmem_st16(tmem + lane_off + PC + 64u * (uint32_t)h + 32u + 16u * (uint32_t)hh, lo);
+                mt_tmem_st16(pbuf + 16u * (uint32_t)hh, &sv[16 * hh]);
+                mt_tmem_st16(pbuf + 32u + 16u * (uint32_t)hh, lo);
             }
             mt_tc_fence_before();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(pfull);
+            // P V of block i - 1 into the output, while P V of block i runs; its TMEM
+            // buffer is next written by P V of block i + 1, after pfull(i + 1)
+            if (i >= 1) fold(i - 1, a_prev);
+            a_prev = alpha;
         }
-        if (ok && mt_mbar_wait(pempty, (uint32_t)(nb - 1) & 1u, abort_flag, status, 4)) {
-            mt_tc_fence_after();
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                float t[16];
-                mt_tmem_ld16(tmem + lane_off + OC + 32u * (uint32_t)h + 16u * (uint32_t)hh, t);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) o[16 * hh + j] = fmaf(o[16 * hh + j], a_prev, t[j]);
-            }
+        if (ok && mt_mbar_wait(pempty, (uint32_t)(nb - 1) & 1u, abort_flag, status, 4)) fold(nb - 1, a_prev);
+        else ok = false;
+        if (ok) {
             const float lt = __fadd_rn(l, exchange(nb, l));
             const int row = q0 + r;
             if (ok && row < Sq) {

@@ -208,8 +208,8 @@ class TcAttentionFragment:
         )
 
 
-# mt_fa_layout::kBytes (Q 32 KB + two 64 KB K/V stages + half-row exchange + barriers) plus
-# 1 KB for aligning the arena to the 128-byte swizzle atom.
+# mt_fa_layout::kBytes (Q / Q lo 32 KB + two 64 KB K/V stages + half-row exchange +
+# barriers) plus 1 KB for aligning the arena to the 128-byte swizzle atom.
 TC_ARENA_FLOATS = (32768 + 2 * 65536 + 2048 + 32 * 8 + 16 + 1024) // 4
 
 

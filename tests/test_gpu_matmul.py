@@ -86,3 +86,54 @@ def test_diamond_shared_a(cuda_device, monkeypatch, pipe):
     r64 = evaluate(ops, np.float64)
     r32 = evaluate(ops, np.float32)
     assert_matmul_close(res.env["z"], r64["z"], r32["z"], what=f"diamond {pipe}")
+
+
+def _gated(M, K, N, transpose_b=False, seed=0):
+    """act(A @ W1 + b1) * (A @ W3): the dual-GEMM epilogue DAG (GELU-tanh gate)."""
+    r = np.random.default_rng(seed)
+    ops = Operations()
+    ops.from_numpy(r.normal(0, 1, (M, K)).astype(np.float32), "A")
+    for w in ("W1", "W3"):
+        if transpose_b:
+            ops.from_numpy(r.normal(0, K ** -0.5, (N, K)).astype(np.float32), w + "t")
+            ops.transpose(w + "t", out=w)
+        else:
+            ops.from_numpy(r.normal(0, K ** -0.5, (K, N)).astype(np.float32), w)
+    ops.from_numpy(r.normal(0, 0.02, (1, N)).astype(np.float32), "b1")
+    ops.matmul(a="A", b="W1", out="z1")
+    ops.elementwise("add", out="z1b", operands=("z1", "b1"), y_broadcast="row")
+    ops.elementwise("mul", out="c", operands=("z1b", "z1b"))
+    ops.elementwise("mul", out="c3", operands=("c", "z1b"))
+    ops.elementwise("mul", out="k", operands=("c3", 0.044715))
+    ops.elementwise("add", out="u", operands=("z1b", "k"))
+    ops.elementwise("mul", out="v", operands=("u", 0.7978845608))
+    ops.elementwise("tanh", out="t", operands=("v",))
+    ops.elementwise("add", out="t1", operands=("t", 1.0))
+    ops.elementwise("mul", out="hz", operands=("z1b", 0.5))
+    ops.elementwise("mul", out="g", operands=("hz", "t1"))
+    ops.matmul(a="A", b="W3", out="z3")
+    ops.elementwise("mul", out="U", operands=("g", "z3"))
+    return ops
+
+
+@pytest.mark.parametrize("M,K,N,tb", [(256, 256, 512, False), (200, 96, 96, False), (384, 512, 256, True),
+                                      (130, 160, 320, True)])
+def test_dual_gemm_epilogue(cuda_device, M, K, N, tb):
+    ops = _gated(M, K, N, transpose_b=tb, seed=M + N)
+    res = run(ops)
+    assert [g.strategy.value for g in res.groups] == ["dual_gemm_epilogue"]
+    assert res.groups[0].pipe == "tcgen05"
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env["U"], r64["U"], r32["U"], what=f"dual {M}x{K}x{N} tb={tb}")
+
+
+@pytest.mark.parametrize("K", [2048, 4096])
+def test_tc_matmul_long_k(cuda_device, K):
+    """Long reductions: the per-32 chunk promotion keeps the error at fp32-dot level."""
+    ops, out = _mm(256, K, 256, seed=K)
+    res = run(ops)
+    assert res.groups[0].pipe == "tcgen05"
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env[out], r64[out], r32[out], what=f"K={K}")
