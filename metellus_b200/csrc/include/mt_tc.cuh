@@ -47,7 +47,7 @@ __device__ __forceinline__ void mt_mbar_expect_tx(uint64_t* bar, uint32_t bytes)
 __device__ __forceinline__ bool mt_mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                  "selp.b32 %0, 1, 0, p;\n\t}"
                  : "=r"(ok) : "r"(mt_smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
