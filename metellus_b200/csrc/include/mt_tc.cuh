@@ -80,6 +80,60 @@ __device__ __forceinline__ void mt_mbar_drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// ---- thread-block clusters (split-K pairs) ---------------------------------------
+
+__device__ __forceinline__ uint32_t mt_cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mt_cluster_map(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(mt_smem_u32(p)), "r"(rank));
+    return a;
+}
+__device__ __forceinline__ void mt_st_cluster_v4(uint32_t addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};"
+                 :: "r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w) : "memory");
+}
+// Arrive on an mbarrier in another cluster CTA's shared memory; release at cluster
+// scope, so this thread's earlier shared::cluster stores are visible to its waiters.
+__device__ __forceinline__ void mt_mbar_arrive_remote(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mt_mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(mt_smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait for arrivals from another cluster CTA (acquire at cluster scope). With
+// `ignore_abort` the wait runs to its time limit even when this CTA is aborting: a
+// split-K partner keeps its shared memory alive until the remote arrive it expects.
+__device__ __forceinline__ bool mt_mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                     int* status, int code, bool ignore_abort) {
+    const uint64_t t0 = mt_globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mt_mbar_try_wait_cluster(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (!ignore_abort && *abort_flag) return false;
+            if (mt_globaltimer() - t0 > MT_WAIT_LIMIT_NS) {
+                if (status) atomicCAS(status, 0, code);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+// Cluster-wide barrier: every thread of both CTAs executes it right after set-up
+// (mbarrier initialisation), before any role can wait on anything.
+__device__ __forceinline__ void mt_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // Prologue / epilogue adaptors around lambdas generated per kernel.
 template <class F>
 struct mt_prologue {
@@ -285,7 +339,7 @@ struct mt_gemm_layout {
     static constexpr uint32_t kStageBytes = kABytes + (uint32_t)NB * kBSlots * kBBytes;
     static constexpr uint32_t kTileBytes = STAGES * kStageBytes;
     static constexpr uint32_t kBarOffset = kTileBytes;              // full, conv, empty per stage + accum
-    static constexpr uint32_t kBytes = kTileBytes + (3 * STAGES + 4) * 8 + 16;
+    static constexpr uint32_t kBytes = kTileBytes + (3 * STAGES + 6) * 8 + 16;
 };
 
 // K-major 128-byte-swizzled operand tile (rows of 32 fp32 = 128 B, 8-row atoms of
@@ -430,7 +484,16 @@ __device__ __forceinline__ void mt_convert_a_rows(const float* tile, uint32_t t_
 // buffer (double buffered), and the accumulator warps add every finished chunk into
 // fp32 registers with round-to-nearest adds, which keeps the normwise error at the
 // level of an fp32 dot product.
-template <int BN, int STAGES, bool A_MN, bool B_MN, int NB, class ProA, class ProB, class Epi, int CHUNK = 1>
+//
+// Split-K (SPLITK = 2): the launch is in clusters of two CTAs along x that share one
+// output tile; CTA rank r runs the r-th half of the k-tiles. Rank 0's accumulator
+// warps, once their mainloop is done, signal rank 1 (remote mbarrier arrive); rank 1
+// writes its fp32 partial sums into rank 0's (now free) stage memory through
+// distributed shared memory and signals back; rank 0 adds them (fixed order: its own
+// half first) and runs the epilogue. Used when the output has too few tiles to fill
+// the SMs (C = 1024^3: 64 tiles of 128 x 128 -> 128 CTAs).
+template <int BN, int STAGES, bool A_MN, bool B_MN, int NB, int SPLITK = 1, class ProA, class ProB, class Epi,
+          int CHUNK = 1>
 __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                int M, int N, int K, const ProA& proA, const ProB& proB,
                                                const Epi& epi, int* status, void* smem_raw) {
@@ -443,6 +506,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     static_assert(BN == 64 || BN == 128, "BN must be 64 or 128");
     static_assert(NB * BN <= 256, "one MMA covers every anchor: N = NB * BN <= 256");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
+    static_assert(SPLITK == 1 || (SPLITK == 2 && NB == 1), "split-K pairs: one anchor");
+    static_assert(SPLITK == 1 || 128u * NB * BN * 4u <= L::kTileBytes, "partial sums must fit the stage memory");
     constexpr int NCONV = 6;
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -451,7 +516,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     uint64_t* empty = conv + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2]
     uint64_t* tempty = tfull + 2;       // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* xready = tempty + 2;      // split-K: rank 0's stage memory is free (on rank 1)
+    uint64_t* xfull = xready + 1;       // split-K: rank 1's partial sums landed (on rank 0)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
@@ -460,11 +527,12 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     // and each B column block is fetched from DRAM about once per group instead of
     // once per M tile (row-major order streams all of B once per M tile when B does
     // not fit L2).
+    const int rank = SPLITK > 1 ? (int)mt_cluster_rank() : 0;
     int m0, n0;
     {
         constexpr int kGroupM = 8;
-        const int n_tiles = (int)gridDim.x, m_tiles = (int)gridDim.y;
-        const int id = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+        const int n_tiles = (int)gridDim.x / SPLITK, m_tiles = (int)gridDim.y;
+        const int id = (int)(blockIdx.y * n_tiles + blockIdx.x / SPLITK);
         const int group = id / (kGroupM * n_tiles);
         const int first_m = group * kGroupM;
         const int gsize = min(m_tiles - first_m, kGroupM);
@@ -472,7 +540,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         m0 = (first_m + in_group % gsize) * 128;
         n0 = (in_group / gsize) * BN;
     }
-    const int nk = (K + 31) / 32;
+    // this CTA's k-tiles: [kbeg, kbeg + nk) of ceil(K / 32)
+    const int nk_all = (K + 31) / 32;
+    const int per = (nk_all + SPLITK - 1) / SPLITK;
+    const int kbeg = SPLITK > 1 ? rank * per : 0;
+    const int nk = SPLITK > 1 ? max(0, min(nk_all, kbeg + per) - kbeg) : nk_all;
     const int nchunks = (nk + CHUNK - 1) / CHUNK;
     auto A_raw = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
     // B tiles of all anchors side by side (hi: anchor 0, anchor 1; then lo likewise),
@@ -496,6 +568,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
             mt_mbar_init(&tfull[b], 1);
             mt_mbar_init(&tempty[b], 8);
         }
+        mt_mbar_init(xready, 256);
+        mt_mbar_init(xfull, 256);
         *abort_flag = 0;
         mt_fence_barrier_init();
     }
@@ -507,6 +581,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     if (warp == 1) mt_tmem_alloc(tmem_slot, NCOLS);
     mt_tc_fence_before();
     __syncthreads();
+    if constexpr (SPLITK > 1) mt_cluster_sync();  // partner's barriers initialised
     mt_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -518,11 +593,12 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                 const uint32_t round = (uint32_t)(kt / STAGES);
                 if (kt >= STAGES && !mt_mbar_wait(&empty[s], (round - 1) & 1u, abort_flag, status, 1)) break;
                 mt_mbar_expect_tx(&full[s], L::kABytes + NB * L::kBBytes);
-                mt_tma_load_2d(A_raw(s), tmA, &full[s], kt * 32, m0);
+                const int kg = (kbeg + kt) * 32;
+                mt_tma_load_2d(A_raw(s), tmA, &full[s], kg, m0);
                 for (int b = 0; b < NB; ++b) {
                     const mt_tmap* tb = b == 0 ? tmB0 : tmB1;
-                    if (B_MN) mt_tma_load_3d(B_dst(s, b), tb, &full[s], 0, kt * 32, n0 / 32);
-                    else mt_tma_load_2d(B_dst(s, b), tb, &full[s], kt * 32, n0);
+                    if (B_MN) mt_tma_load_3d(B_dst(s, b), tb, &full[s], 0, kg, n0 / 32);
+                    else mt_tma_load_2d(B_dst(s, b), tb, &full[s], kg, n0);
                 }
                 issued = kt + 1;
             }
@@ -573,11 +649,13 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
             const int s = kt % STAGES;
             if (!mt_mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 3)) break;
             if (warp >= 4)
-                mt_convert_a_rows(A_raw(s), tmem + ACOLS + 64u * (uint32_t)s, warp & 3, lane, m0, kt * 32, M, K, proA);
+                mt_convert_a_rows(A_raw(s), tmem + ACOLS + 64u * (uint32_t)s, warp & 3, lane, m0, (kbeg + kt) * 32, M, K,
+                                  proA);
             // The split is elementwise, so it runs in place whatever the swizzle; the
             // prologue (coordinates) is only supported on K-major B tiles.
             for (int b = 0; b < NB; ++b)
-                mt_convert_tile<false, false, BN, NCONV * 32>(B_hi(s, b), B_lo(s, b), n0, kt * 32, N, K, proB, ct);
+                mt_convert_tile<false, false, BN, NCONV * 32>(B_hi(s, b), B_lo(s, b), n0, (kbeg + kt) * 32, N, K, proB,
+                                                              ct);
             mt_fence_proxy_async();
             mt_tc_fence_before();
             __syncwarp();
@@ -612,6 +690,37 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
             mt_tc_fence_before();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(&tempty[tb]);
+        }
+        if constexpr (SPLITK > 1) {
+            const int t = (warp - 8) * 32 + lane;                // 0..255
+            float4* xbuf = reinterpret_cast<float4*>(smem);      // stage memory, free after the mainloop
+            if (rank == 1) {
+                // wait until rank 0's stages are free, even when aborting (keeps this
+                // CTA alive for rank 0's remote arrive)
+                const bool ready = mt_mbar_wait_cluster(xready, 0, abort_flag, status, 6, true);
+                if (ok && ready) {
+#pragma unroll
+                    for (int g = 0; g < HALF / 4; ++g)
+                        mt_st_cluster_v4(mt_cluster_map(&xbuf[g * 256 + t], 0),
+                                         make_float4(acc[0][4 * g], acc[0][4 * g + 1], acc[0][4 * g + 2],
+                                                     acc[0][4 * g + 3]));
+                    mt_mbar_arrive_remote(mt_cluster_map(xfull, 0));
+                }
+                ok = false;  // rank 0 runs the epilogue
+            } else if (ok) {
+                mt_mbar_arrive_remote(mt_cluster_map(xready, 1));
+                ok = mt_mbar_wait_cluster(xfull, 0, abort_flag, status, 7, false);
+                if (ok) {
+#pragma unroll
+                    for (int g = 0; g < HALF / 4; ++g) {
+                        const float4 p = xbuf[g * 256 + t];
+                        acc[0][4 * g] = __fadd_rn(acc[0][4 * g], p.x);
+                        acc[0][4 * g + 1] = __fadd_rn(acc[0][4 * g + 1], p.y);
+                        acc[0][4 * g + 2] = __fadd_rn(acc[0][4 * g + 2], p.z);
+                        acc[0][4 * g + 3] = __fadd_rn(acc[0][4 * g + 3], p.w);
+                    }
+                }
+            }
         }
         if (ok) {
             const int row = m0 + q * 32 + lane;

@@ -98,19 +98,30 @@ def _stage_bytes(bn: int, nb: int, b_mn: bool) -> int:
     return 128 * 32 * 4 + nb * 2 * bn * 32 * 4
 
 
-def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True) -> tuple[int, int]:
-    """(BN, stages): the widest N tile that still gives ~one CTA per SM, and as many
-    pipeline stages as fit the shared-memory budget and tensor memory (512 columns:
-    two accumulator chunks of nb * BN columns, plus 64 columns of A hi / lo per stage)."""
+def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True, K: int = 0) -> tuple[int, int, int]:
+    """(BN, stages, split-K): the widest N tile that still gives ~one CTA per SM, and
+    as many pipeline stages as fit the shared-memory budget and tensor memory (512
+    columns: two accumulator chunks of nb * BN columns, plus 64 columns of A hi / lo
+    per stage). A k-tile costs about the same time at BN = 64 as at 128 (the A split
+    and the pipeline hand-offs dominate), so an output with too few 128-wide tiles to
+    fill the SMs keeps BN = 128 and splits K over a two-CTA cluster instead of halving
+    BN (C = 1024^3: 64 tiles -> 128 CTAs of 16 k-tiles each)."""
     tiles_m = -(-M // 128)
-    bn = 128 if nb == 1 and tiles_m * -(-N // 128) >= SM_COUNT * 0.8 else 64
+    tiles128 = tiles_m * -(-N // 128)
+    splitk = 1
+    if nb == 1 and tiles128 >= SM_COUNT * 0.8:
+        bn = 128
+    elif nb == 1 and 2 * tiles128 <= SM_COUNT and -(-K // 32) >= 16:
+        bn, splitk = 128, 2
+    else:
+        bn = 64
     tmem_stages = (512 - 2 * nb * bn) // 64
     stages = max(2, min(6, tmem_stages, SMEM_BUDGET // _stage_bytes(bn, nb, b_mn)))
-    return bn, stages
+    return bn, stages, splitk
 
 
 def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
-    return stages * _stage_bytes(bn, nb, b_mn) + (3 * stages + 4) * 8 + 16 + 1024
+    return stages * _stage_bytes(bn, nb, b_mn) + (3 * stages + 6) * 8 + 16 + 1024
 
 
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
@@ -162,6 +173,7 @@ class TcGemmFragment:
     pro_a: str | None           # expression in (x, r, c) or None
     pro_b: str | None
     epi_body: str               # body of the per-(row, 32 columns) store lambda
+    splitk: int = 1             # 2: two-CTA cluster per tile, K halves combined via DSMEM
     name: str = "tc_gemm"
     kind: str = "compute"
 
@@ -183,7 +195,8 @@ class TcGemmFragment:
         tb1 = "&tm_b1" if self.nb > 1 else "&tm_b0"
         lines.append(
             f"mt_gemm_3xtf32<{self.bn}, {self.stages}, {str(self.a_mn).lower()}, {str(self.b_mn).lower()}, "
-            f"{self.nb}>(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);"
+            f"{self.nb}, {self.splitk}>(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, "
+            "tc_arena);"
         )
         return "\n".join(lines)
 
@@ -269,7 +282,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
         for o in op.inputs:
             if o.name not in {e.out.name for e in decision.epilogue} and o.name != anchor.out.name:
                 extras.add_tensor(o, base)
-    bn, stages = _pick_tile(M, N, 1, lb == "mn")
+    bn, stages, splitk = _pick_tile(M, N, 1, lb == "mn", K)
     need_col_check = N % 32 != 0
     epi = _epi_function(decision.epilogue, {anchor.out.name: "v[0][J]"}, out_key,
                         final_out.name, N, N, need_col_check)
@@ -281,7 +294,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
         _tmap(bindings.index(src_b.buffer_key), src_b, lb, bn),
     )
     frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=1, pro_a=pro_a,
-                          pro_b=pro_b, epi_body=epi)
+                          pro_b=pro_b, epi_body=epi, splitk=splitk)
     n_arena = _smem_bytes(bn, stages, 1, lb == "mn") // 4
     fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
     ctx = CodegenContext(
@@ -294,8 +307,9 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     del nparams
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
-        grid=(-(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
+        grid=(splitk * -(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
+        cluster_x=splitk,
     )
 
 
@@ -341,7 +355,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
         for o in op.inputs:
             if o.name not in inside:
                 extras.add_tensor(o, out_slot + 1)
-    bn, stages = _pick_tile(M, N, 2, lb == "mn")
+    bn, stages, _ = _pick_tile(M, N, 2, lb == "mn", K)
     epi = _epi_function(tuple(epi_ops), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key,
                         merge.out.name, N, N, N % 32 != 0)
     bindings = (*in_keys, out_key, *extras.bindings)

@@ -146,7 +146,8 @@ class CheckStatus:
         if words.any():
             raise RuntimeError(
                 f"kernel status {words[:4].tolist()}: a device-side wait timed out "
-                "(1=producer, 2=mma, 3=converter, 4=epilogue); results are invalid"
+                "(1=producer, 2=mma, 3=converter, 4=softmax, 5=accumulator, 6/7=split-K exchange); "
+                "results are invalid"
             )
 
 

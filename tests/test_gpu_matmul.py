@@ -137,3 +137,16 @@ def test_tc_matmul_long_k(cuda_device, K):
     r64 = evaluate(ops, np.float64)
     r32 = evaluate(ops, np.float32)
     assert_matmul_close(res.env[out], r64[out], r32[out], what=f"K={K}")
+
+
+@pytest.mark.parametrize("M,K,N", [(1024, 1024, 1024), (512, 4096, 512), (200, 1000, 320), (256, 520, 384)])
+def test_tc_matmul_split_k_pairs(cuda_device, M, K, N):
+    """Few output tiles: a two-CTA cluster per tile splits K and combines the halves
+    through distributed shared memory (odd k-tile counts and ragged edges included)."""
+    ops, out = _mm(M, K, N, bias=True, relu=True, seed=M + K)
+    res = run(ops)
+    g = res.groups[0]
+    assert g.pipe == "tcgen05" and g.cluster_x == 2, (g.pipe, g.cluster_x)
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env[out], r64[out], r32[out], what=f"split-K {M}x{K}x{N}")
