@@ -240,8 +240,14 @@ def main() -> None:
     from metellus_b200.runtime import backend
     from metellus_b200.runtime.buffer import Buffer
 
-    distributed.init()  # binds the GPU; for N > 1 also creates the NCCL communicator
+    def trace(msg: str) -> None:
+        if os.environ.get("METELLUS_TRACE"):
+            print(f"[rank {rank}] {msg}", file=sys.stderr, flush=True)
+
     key = args.config
+    # binds the GPU; for N > 1 and a combined reduction also creates the NCCL communicator
+    distributed.init(nccl=key == "c3sum")
+    trace("device and communicator ready")
     shape = shard_shape(key)
     for kv in filter(None, args.shape.split(",")):
         k, v = kv.split("=")
@@ -277,9 +283,11 @@ def main() -> None:
         if dist is not None:
             dist.barrier()
 
+    trace("compiled and allocated")
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
+    trace("warm-up done")
     # Timed steps replay the dispatch list from a CUDA graph (captured after the
     # warm-up has loaded every module), so a step is one graph launch and the host
     # stays ahead of the device; per-kernel times come from a second, per-dispatch pass.
@@ -376,7 +384,9 @@ def main() -> None:
 
     e2e = None
     if not (args.no_e2e or args.profile):
+        trace("timed steps done")
         e2e = run_e2e(ops, groups, key, shape, world, args, dist, barrier)
+        trace("e2e done")
 
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu or args.profile):
@@ -402,6 +412,7 @@ def main() -> None:
     if dist is not None:
         dist.barrier()
         distributed.shutdown()
+        trace("communicator destroyed")
         dist.destroy_process_group()
 
 
@@ -469,12 +480,20 @@ def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
     inputs = {n: p.array for n, p in pinned.items()}
     outs = {out_name: out_host.array}
 
+    # programs with an NCCL combine wait for the device at the end of every step (an
+    # 8-rank run that queued such steps back to back without waiting stalled)
+    wait_each = any("nccl" in (g.pipe or "") for g in exe.groups)
+
     def step():
-        exe(inputs, out=outs, wait=False)
+        exe(inputs, out=outs, wait=wait_each)
 
     steps = max(3, min(args.steps, 10))
-    for _ in range(3):
+    trace = os.environ.get("METELLUS_TRACE")
+    for i in range(3):
         step()
+        if trace:
+            exe.synchronize()
+            print(f"[rank {os.environ.get('RANK', '0')}] e2e warm-up step {i} done", file=sys.stderr, flush=True)
     exe.synchronize()
     barrier()
     e0, e1 = backend.Event(), backend.Event()

@@ -63,15 +63,15 @@ def exchange_nccl_id(info: RankInfo, group=None, make_id=None) -> bytes:
     return obj[0]
 
 
-def init(group=None) -> RankInfo:
-    """Bind this process to its GPU and, for more than one rank, create the NCCL
-    communicator the combining reductions use (torch.distributed must already be
-    initialised then)."""
+def init(group=None, *, nccl: bool = True) -> RankInfo:
+    """Bind this process to its GPU and, for more than one rank and ``nccl``, create the
+    NCCL communicator the combining reductions use (torch.distributed must already be
+    initialised then). Programs without a combined reduction pass ``nccl=False``."""
     global _nccl_ready
     info = rank_info()
     backend.set_device(info.local_rank)
     backend.init()
-    if info.world > 1 and not _nccl_ready:
+    if nccl and info.world > 1 and not _nccl_ready:
         backend.nccl_init(info.world, info.rank, exchange_nccl_id(info, group))
         _nccl_ready = True
     return info
