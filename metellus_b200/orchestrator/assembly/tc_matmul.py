@@ -288,7 +288,6 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
                         final_out.name, N, N, need_col_check)
     bindings = (*in_slots.keys(), out_key, *extras.bindings)
     params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
-    nparams = len(bindings) + 1
     tmaps = (
         _tmap(bindings.index(src_a.buffer_key), src_a, la, 128),
         _tmap(bindings.index(src_b.buffer_key), src_b, lb, bn),
@@ -304,7 +303,6 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
         extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0"),
         min_blocks_per_sm=1,
     )
-    del nparams
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
         grid=(splitk * -(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
