@@ -140,6 +140,9 @@ def classify(vertex: Vertex) -> DecisionView:
     post = tuple(op for op in ops[idx + 1:] if isinstance(op, ElementwiseOp))
 
     if isinstance(anchor, MatmulOp):
+        final = post[-1].out.name if post else anchor.out.name
+        extra = set(outs) - {final}
+        assert not extra, f"matmul vertex must materialise only its final output; also needs {sorted(extra)}"
         pa = trace_prologue(anchor.a.name, pre)
         pb = trace_prologue(anchor.b.name, pre)
         if post and all(is_lane_agnostic_pred(e) for e in post):
@@ -161,6 +164,10 @@ def classify(vertex: Vertex) -> DecisionView:
                           and post[0].operands[0].name == anchor.out.name
                           and is_linear_chain(post)))
         and all(len(e.out.matrix_shape) == 1 for e in post)
+        # the reference reduction templates store only the final value; a vertex that
+        # must also materialise a prologue or intermediate value (built by the B200 row
+        # pass when that value has another consumer) runs row-resident
+        and set(outs) <= {(post[-1].out.name if post else anchor.out.name)}
     )
     if not reference_shaped:
         return DecisionView(strategy=FusionStrategy.ROW_RESIDENT, ops=ops, outputs=outs)

@@ -88,3 +88,21 @@ def test_non_finite_values_propagate(cuda_device):
     ops2.elementwise("add", out="b", operands=("a", 1.0))
     res2 = run(ops2)
     np.testing.assert_array_equal(res2.env["b"], evaluate(ops2, np.float32)["b"])  # inf, nan kept
+
+
+def test_row_fused_value_with_second_consumer(cuda_device):
+    """A value the row pass fuses into a reduction's kernel but that another kernel
+    also reads (here t0, read by the reduction and by the matmul prologue) must still
+    be written to memory (found by the planner property test)."""
+    r = np.random.default_rng(2220)
+    ops = Operations()
+    ops.from_numpy(r.normal(size=(64, 128)).astype(np.float32), "x0")
+    ops.from_numpy(r.normal(size=(128, 64)).astype(np.float32), "W")
+    ops.elementwise("max", out="t0", operands=("x0", "x0"))
+    ops.reduction("max", out="r", x="t0", axis=-1)
+    ops.reshape("r", (64, 1), out="rc")
+    ops.elementwise("subtract", out="t1", operands=("t0", "rc"), y_broadcast="col")
+    ops.matmul(a="t1", b="W", out="t3")
+    res = run(ops)
+    r64, r32 = evaluate(ops, np.float64), evaluate(ops, np.float32)
+    assert_matmul_close(res.env["t3"], r64["t3"], r32["t3"], what="row-fused second consumer")

@@ -35,15 +35,16 @@ def random_program(seed: int) -> Operations:
     for i in range(int(r.integers(2, 4))):
         ops.from_numpy(r.normal(size=(M, N)).astype(np.float32), f"x{i}")
         mats.append(f"x{i}")
-    shapes = {"bias": (1, N), "W": (N, P), "W2": (N, P)}
+    shapes = {"bias": (1, N), "W": (N, P), "W2": (N, P), "WT": (P, N)}
 
     def need(name: str) -> str:  # inputs are declared on first use (every upload must be read)
         if name not in ops.tensors:
             ops.from_numpy(r.normal(size=shapes[name]).astype(np.float32), name)
         return name
     for k in range(int(r.integers(3, 11))):
-        kind = r.choice(["unary", "binary", "scalar", "rowb", "softmaxish", "matmul", "diamond", "gated", "onp"],
-                        p=[0.17, 0.17, 0.12, 0.08, 0.12, 0.08, 0.08, 0.1, 0.08])
+        kind = r.choice(["unary", "binary", "scalar", "rowb", "softmaxish", "matmul", "diamond", "gated", "onp",
+                         "tmatmul"],
+                        p=[0.16, 0.16, 0.11, 0.08, 0.12, 0.08, 0.08, 0.1, 0.06, 0.05])
         out = f"t{k}"
         if kind == "unary":
             ops.elementwise(str(r.choice(UNARY)), out=out, operands=(str(r.choice(mats)),))
@@ -81,6 +82,11 @@ def random_program(seed: int) -> Operations:
             ops.elementwise("mul", out=f"{out}_h", operands=(f"{out}_c", f"{out}_t"))
             ops.matmul(a=src, b=need("W2"), out=f"{out}_b")
             ops.elementwise("mul", out=out, operands=(f"{out}_h", f"{out}_b"))
+            others[out] = (M, P)
+        elif kind == "tmatmul":  # B as a transposed view of a (P, N) input
+            if "WTt" not in ops.tensors:
+                ops.transpose(need("WT"), out="WTt")
+            ops.matmul(a=str(r.choice(mats)), b="WTt", out=out)
             others[out] = (M, P)
         elif others:  # an elementwise op over (M, P) results
             a = str(r.choice(list(others)))
