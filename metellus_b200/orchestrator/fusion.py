@@ -108,6 +108,20 @@ def _is_dual_gemm_vertex(vertex: Vertex) -> bool:
     return classify(vertex).strategy is FusionStrategy.DUAL_GEMM_EPILOGUE
 
 
+def _is_chain_vertex(vertex: Vertex) -> bool:
+    """An elementwise vertex whose ops form a linear chain (each op's primary operand is
+    the previous op's output) -- the only elementwise shape the reference passes ever
+    build, and the only one its prologue / epilogue templates evaluate. The B200
+    elementwise-DAG pass builds other shapes; those are not absorbed into anchors."""
+    if not _is_elementwise_vertex(vertex):
+        return False
+    for prev, cur in zip(vertex.ops, vertex.ops[1:]):
+        p = cur.operands[0]
+        if not (isinstance(p, Tensor) and p.name == prev.out.name):
+            return False
+    return True
+
+
 def _is_elementwise_vertex(vertex: Vertex) -> bool:
     return len(vertex.ops) > 0 and all(isinstance(op, ElementwiseOp) for op in vertex.ops)
 
@@ -156,7 +170,7 @@ def try_epilogue_absorb(graph: Graph, blacklist: frozenset[frozenset[int]]) -> G
         if len(cons) != 1:
             continue
         v = cons[0]
-        if not _is_elementwise_vertex(v):
+        if not _is_chain_vertex(v):
             continue
         head = v.ops[0]
         if isinstance(anchor, MatmulOp):
@@ -207,7 +221,7 @@ def _merge_in_order(graph: Graph, *vertices: Vertex) -> tuple[Op, ...]:
 def try_prologue_absorb_single(graph: Graph, blacklist: frozenset[frozenset[int]]) -> Graph | None:
     """elem V -> anchor vertex A (unique consumer) into A's load transform."""
     for v in graph.vertices:
-        if not _is_elementwise_vertex(v):
+        if not _is_chain_vertex(v):
             continue
         tail = v.ops[-1].out.name
         if tail not in v.outputs:

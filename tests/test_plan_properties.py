@@ -24,8 +24,11 @@ UNARY = ("negate", "exp", "tanh", "absolute", "sqrt", "recip")
 BINARY = ("add", "subtract", "mul", "max", "min")
 
 
-def random_program(seed: int) -> Operations:
+def random_program(seed: int, safe: bool = False) -> Operations:
+    """A seeded random program; ``safe`` keeps values finite and O(1) (no exp / sqrt /
+    recip, sums instead of maxima) for numeric checks on the GPU."""
     r = np.random.default_rng(seed)
+    unary = ("negate", "tanh", "absolute") if safe else UNARY
     M = int(r.choice([32, 64, 96]))
     N = int(r.choice([32, 64, 128]))
     P = int(r.choice([32, 64]))
@@ -47,7 +50,7 @@ def random_program(seed: int) -> Operations:
                         p=[0.16, 0.16, 0.11, 0.08, 0.12, 0.08, 0.08, 0.1, 0.06, 0.05])
         out = f"t{k}"
         if kind == "unary":
-            ops.elementwise(str(r.choice(UNARY)), out=out, operands=(str(r.choice(mats)),))
+            ops.elementwise(str(r.choice(unary)), out=out, operands=(str(r.choice(mats)),))
             mats.append(out)
         elif kind == "binary":
             a, b = r.choice(mats, 2)
@@ -61,7 +64,7 @@ def random_program(seed: int) -> Operations:
             mats.append(out)
         elif kind == "softmaxish":
             src = str(r.choice(mats))
-            ops.reduction(str(r.choice(["max", "sum"])), out=f"{out}_r", x=src, axis=-1)
+            ops.reduction(str(r.choice(["max", "min"] if safe else ["max", "sum"])), out=f"{out}_r", x=src, axis=-1)
             ops.reshape(f"{out}_r", (M, 1), out=f"{out}_c")
             ops.elementwise("subtract", out=out, operands=(src, f"{out}_c"), y_broadcast="col")
             mats.append(out)
@@ -90,9 +93,9 @@ def random_program(seed: int) -> Operations:
             others[out] = (M, P)
         elif others:  # an elementwise op over (M, P) results
             a = str(r.choice(list(others)))
-            ops.elementwise(str(r.choice(UNARY)), out=out, operands=(a,))
+            ops.elementwise(str(r.choice(unary)), out=out, operands=(a,))
             others[out] = (M, P)
-    used = {t.name for op in ops.build() for t in op.inputs}
+    used = {t.buffer_key for op in ops.build() for t in op.inputs}
     for i, name in enumerate(n for n in list(ops.uploads) if n not in used):
         ops.elementwise("add", out=f"u{i}", operands=(name, mats[-1]))
     return ops
