@@ -35,9 +35,10 @@ def _depends_on_matmul(ops, name: str) -> bool:
     return False
 
 
-@pytest.mark.parametrize("seed", range(24))
-def test_random_program_matches_oracle(cuda_device, seed):
-    ops = random_program(seed * 7919 + 11, safe=True)
+@pytest.mark.parametrize("large", [False, True], ids=["simt", "tcgen05"])
+@pytest.mark.parametrize("seed", range(20))
+def test_random_program_matches_oracle(cuda_device, seed, large):
+    ops = random_program(seed * 7919 + 11, safe=True, large=large)
     res = run(ops)
     r64 = evaluate(ops, np.float64)
     r32 = evaluate(ops, np.float32)

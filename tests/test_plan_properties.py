@@ -24,25 +24,33 @@ UNARY = ("negate", "exp", "tanh", "absolute", "sqrt", "recip")
 BINARY = ("add", "subtract", "mul", "max", "min")
 
 
-def random_program(seed: int, safe: bool = False) -> Operations:
+def random_program(seed: int, safe: bool = False, large: bool = False) -> Operations:
     """A seeded random program; ``safe`` keeps values finite and O(1) (no exp / sqrt /
-    recip, sums instead of maxima) for numeric checks on the GPU."""
+    recip, sums instead of maxima) for numeric checks on the GPU; ``large`` picks
+    shapes big enough for the tensor-core (tcgen05) plans."""
     r = np.random.default_rng(seed)
     unary = ("negate", "tanh", "absolute") if safe else UNARY
-    M = int(r.choice([32, 64, 96]))
-    N = int(r.choice([32, 64, 128]))
-    P = int(r.choice([32, 64]))
+    if large:
+        M = int(r.choice([128, 256, 384]))
+        N = int(r.choice([128, 256]))
+        P = int(r.choice([128, 256]))
+    else:
+        M = int(r.choice([32, 64, 96]))
+        N = int(r.choice([32, 64, 128]))
+        P = int(r.choice([32, 64]))
     ops = Operations()
     mats = []          # names of (M, N) tensors
     others = {}        # (M, P) tensors by name
     for i in range(int(r.integers(2, 4))):
         ops.from_numpy(r.normal(size=(M, N)).astype(np.float32), f"x{i}")
+        # weights scaled 1 / sqrt(fan-in) so chained products stay O(1)
         mats.append(f"x{i}")
     shapes = {"bias": (1, N), "W": (N, P), "W2": (N, P), "WT": (P, N)}
 
     def need(name: str) -> str:  # inputs are declared on first use (every upload must be read)
         if name not in ops.tensors:
-            ops.from_numpy(r.normal(size=shapes[name]).astype(np.float32), name)
+            scale = shapes[name][0] ** -0.5 if name in ("W", "W2") else shapes[name][1] ** -0.5 if name == "WT" else 1.0
+            ops.from_numpy((scale * r.normal(size=shapes[name])).astype(np.float32), name)
         return name
     for k in range(int(r.integers(3, 11))):
         kind = r.choice(["unary", "binary", "scalar", "rowb", "softmaxish", "matmul", "diamond", "gated", "onp",
@@ -131,9 +139,9 @@ def _check_plan(ops: Operations, groups) -> None:
 
 
 @settings(max_examples=200, deadline=None)
-@given(st.integers(0, 10**6))
-def test_random_programs_plan_soundly(seed):
-    ops = random_program(seed)
+@given(st.integers(0, 10**6), st.booleans())
+def test_random_programs_plan_soundly(seed, large):
+    ops = random_program(seed, large=large)
     groups = compile_program(ops)
     _check_plan(ops, groups)
     ref_groups = compile_program(ops, b200=False)
