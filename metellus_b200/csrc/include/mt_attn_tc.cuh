@@ -198,12 +198,12 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
             const int s = i & 1;
             const uint32_t par = (uint32_t)(i >> 1) & 1u;
             if (!mt_mbar_wait(&kfull[s], par, abort_flag, status, 3)) break;
-            mt_convert_tile<false, false, 128, 192>(Khi(s), Klo(s), 0, 0, 0, 0, np, ct);
+            mt_convert_tile<false, false, 128, 192>(Khi(s), Khi(s), Klo(s), 0, 0, 0, 0, np, ct);
             mt_fence_proxy_async();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(&kconv[s]);
             if (!mt_mbar_wait(&vfull[s], par, abort_flag, status, 3)) break;
-            mt_convert_tile<false, false, 128, 192>(Vhi(s), Vlo(s), 0, 0, 0, 0, np, ct);
+            mt_convert_tile<false, false, 128, 192>(Vhi(s), Vhi(s), Vlo(s), 0, 0, 0, 0, np, ct);
             mt_fence_proxy_async();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive(&vconv[s]);

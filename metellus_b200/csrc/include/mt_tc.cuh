@@ -328,18 +328,21 @@ struct mt_gemm_smem_plan {
     static constexpr uint32_t kBK = 32;
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int NB>
+template <int BN, int RSTAGES, int CSTAGES, bool A_MN, bool B_MN, int NB>
 struct mt_gemm_layout {
     static_assert(!A_MN, "A tiles must be K-major");
     static constexpr uint32_t kABytes = 128u * 32u * 4u;            // 16 KB
     static constexpr uint32_t kBBytes = (uint32_t)BN * 32u * 4u;
-    // Per stage: A (TMA target; its tf32 hi / lo split goes to tensor memory), then per
-    // anchor b: B hi (TMA target, split in place), B lo.
-    static constexpr uint32_t kBSlots = 2u;
-    static constexpr uint32_t kStageBytes = kABytes + (uint32_t)NB * kBSlots * kBBytes;
-    static constexpr uint32_t kTileBytes = STAGES * kStageBytes;
-    static constexpr uint32_t kBarOffset = kTileBytes;              // full, conv, empty per stage + accum
-    static constexpr uint32_t kBytes = kTileBytes + (3 * STAGES + 6) * 8 + 16;
+    // Raw ring (TMA targets): A, then B of every anchor side by side.
+    static constexpr uint32_t kRawBytes = kABytes + (uint32_t)NB * kBBytes;
+    // Converted ring (MMA operands): B hi of every anchor side by side, then B lo. A's
+    // hi / lo split goes to tensor memory (one 64-column slot per converted stage).
+    static constexpr uint32_t kConvBytes = 2u * (uint32_t)NB * kBBytes;
+    static constexpr uint32_t kRawOffset = 0;
+    static constexpr uint32_t kConvOffset = RSTAGES * kRawBytes;
+    static constexpr uint32_t kTileBytes = RSTAGES * kRawBytes + CSTAGES * kConvBytes;
+    static constexpr uint32_t kBarOffset = kTileBytes;  // rfull, rempty per raw stage; cfull, cempty per converted stage; accum
+    static constexpr uint32_t kBytes = kTileBytes + (2 * RSTAGES + 2 * CSTAGES + 6) * 8 + 16;
 };
 
 // K-major 128-byte-swizzled operand tile (rows of 32 fp32 = 128 B, 8-row atoms of
@@ -393,10 +396,11 @@ struct mt_no_prologue {
 // Convert one landed tile in two phases so every shared-memory load of the thread is
 // in flight before the first split (the converter is latency bound otherwise): load
 // this thread's IT float4 chunks, then apply the prologue (global coordinates
-// recovered from the swizzled offset), split, and store hi in place and lo.
+// recovered from the swizzled offset), split, and store hi (to `hi`, which may be the
+// landed tile itself) and lo.
 template <bool MN, bool A_SIDE, int ROWS, int NT, class Pro>
-__device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int r0, int k0, int rlim, int klim,
-                                                const Pro& pro, int tid) {
+__device__ __forceinline__ void mt_convert_tile(const float* tile, float* hi, float* lo, int r0, int k0, int rlim,
+                                                int klim, const Pro& pro, int tid) {
     constexpr int N4 = ROWS * 32 / 4;
     constexpr int IT = (N4 + NT - 1) / NT;
     float4 v[IT];
@@ -427,7 +431,7 @@ __device__ __forceinline__ void mt_convert_tile(float* tile, float* lo, int r0, 
         mt_split_tf32(v[j].y, h.y, w.y);
         mt_split_tf32(v[j].z, h.z, w.z);
         mt_split_tf32(v[j].w, h.w, w.w);
-        reinterpret_cast<float4*>(tile)[i] = h;
+        reinterpret_cast<float4*>(hi)[i] = h;
         reinterpret_cast<float4*>(lo)[i] = w;
     }
 }
@@ -474,7 +478,8 @@ __device__ __forceinline__ void mt_convert_a_rows(const float* tile, uint32_t t_
 //   warps 2..7   converters: warps 4..7 split the A rows of their TMEM lane quarter
 //                into tf32 hi / lo in tensor memory (the MMA reads A from there, so
 //                shared memory carries only the TMA write and one read of A); then
-//                all six split the B tiles into hi / lo in place
+//                all six split the B tiles from the raw ring into hi / lo in the
+//                converted ring
 //   warps 8..15  accumulators + epilogue: warp w owns TMEM lane quarter (w % 4) and
 //                half (w - 8) / 4 of the columns of every anchor.
 //
@@ -492,15 +497,15 @@ __device__ __forceinline__ void mt_convert_a_rows(const float* tile, uint32_t t_
 // distributed shared memory and signals back; rank 0 adds them (fixed order: its own
 // half first) and runs the epilogue. Used when the output has too few tiles to fill
 // the SMs (C = 1024^3: 64 tiles of 128 x 128 -> 128 CTAs).
-template <int BN, int STAGES, bool A_MN, bool B_MN, int NB, int SPLITK = 1, class ProA, class ProB, class Epi,
-          int CHUNK = 1>
+template <int BN, int RST, int CST, bool A_MN, bool B_MN, int NB, int SPLITK = 1, class ProA, class ProB,
+          class Epi, int CHUNK = 1>
 __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                int M, int N, int K, const ProA& proA, const ProB& proB,
                                                const Epi& epi, int* status, void* smem_raw) {
-    using L = mt_gemm_layout<BN, STAGES, A_MN, B_MN, NB>;
+    using L = mt_gemm_layout<BN, RST, CST, A_MN, B_MN, NB>;
     constexpr int HALF = BN / 2;                  // columns per accumulator warp per anchor
     constexpr uint32_t ACOLS = 2u * NB * BN;      // two chunk buffers of accumulators
-    constexpr uint32_t TCOLS = ACOLS + 64u * STAGES;  // + A hi / lo per stage
+    constexpr uint32_t TCOLS = ACOLS + 64u * CST;  // + A hi / lo per converted stage
     constexpr uint32_t NCOLS = TCOLS <= 32 ? 32 : TCOLS <= 64 ? 64 : TCOLS <= 128 ? 128 : TCOLS <= 256 ? 256 : 512;
     static_assert(TCOLS <= 512, "accumulators and A stages exceed TMEM");
     static_assert(BN == 64 || BN == 128, "BN must be 64 or 128");
@@ -511,10 +516,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     constexpr int NCONV = 6;
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-    uint64_t* conv = full + STAGES;
-    uint64_t* empty = conv + STAGES;
-    uint64_t* tfull = empty + STAGES;   // [2]
+    uint64_t* rfull = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);  // [RST] TMA landed
+    uint64_t* rempty = rfull + RST;     // [RST] converters done reading the raw stage
+    uint64_t* cfull = rempty + RST;     // [CST] converted operands ready
+    uint64_t* cempty = cfull + CST;     // [CST] MMAs done with the converted stage
+    uint64_t* tfull = cempty + CST;     // [2]
     uint64_t* tempty = tfull + 2;       // [2]
     uint64_t* xready = tempty + 2;      // split-K: rank 0's stage memory is free (on rank 1)
     uint64_t* xfull = xready + 1;       // split-K: rank 1's partial sums landed (on rank 0)
@@ -546,23 +552,27 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     const int kbeg = SPLITK > 1 ? rank * per : 0;
     const int nk = SPLITK > 1 ? max(0, min(nk_all, kbeg + per) - kbeg) : nk_all;
     const int nchunks = (nk + CHUNK - 1) / CHUNK;
-    auto A_raw = [&](int s) { return reinterpret_cast<float*>(smem + s * L::kStageBytes); };
-    // B tiles of all anchors side by side (hi: anchor 0, anchor 1; then lo likewise),
-    // so one MMA with N = NB * BN covers every anchor: anchor b's columns land at
-    // accumulator columns [b * BN, (b + 1) * BN).
-    auto B_slot = [&](int s, int b, int j) {
-        return reinterpret_cast<float*>(smem + s * L::kStageBytes + L::kABytes +
-                                        (j * NB + b) * L::kBBytes);
+    // Raw ring: what TMA writes (A, then B of every anchor). Converted ring: B hi of
+    // every anchor side by side, then B lo, so one MMA with N = NB * BN covers every
+    // anchor (anchor b's columns land at accumulator columns [b * BN, (b + 1) * BN)).
+    // A raw stage is free as soon as it is converted, so TMA runs ahead of the MMAs by
+    // RST + CST stages rather than by the stages the converted operands occupy.
+    auto A_raw = [&](int r) { return reinterpret_cast<float*>(smem + L::kRawOffset + r * L::kRawBytes); };
+    auto B_raw = [&](int r, int b) {
+        return reinterpret_cast<float*>(smem + L::kRawOffset + r * L::kRawBytes + L::kABytes + b * L::kBBytes);
     };
-    auto B_dst = [&](int s, int b) { return B_slot(s, b, 0); };
-    auto B_hi = [&](int s, int b) { return B_slot(s, b, 0); };
-    auto B_lo = [&](int s, int b) { return B_slot(s, b, 1); };
+    auto B_cv = [&](int c, int b, int j) {
+        return reinterpret_cast<float*>(smem + L::kConvOffset + c * L::kConvBytes + (j * NB + b) * L::kBBytes);
+    };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mt_mbar_init(&full[s], 1);
-            mt_mbar_init(&conv[s], NCONV);
-            mt_mbar_init(&empty[s], 1);
+        for (int r = 0; r < RST; ++r) {
+            mt_mbar_init(&rfull[r], 1);
+            mt_mbar_init(&rempty[r], NCONV);
+        }
+        for (int c = 0; c < CST; ++c) {
+            mt_mbar_init(&cfull[c], NCONV);
+            mt_mbar_init(&cempty[c], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mt_mbar_init(&tfull[b], 1);
@@ -589,55 +599,55 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         if (lane == 0) {
             int issued = 0;
             for (int kt = 0; kt < nk; ++kt) {
-                const int s = kt % STAGES;
-                const uint32_t round = (uint32_t)(kt / STAGES);
-                if (kt >= STAGES && !mt_mbar_wait(&empty[s], (round - 1) & 1u, abort_flag, status, 1)) break;
-                mt_mbar_expect_tx(&full[s], L::kABytes + NB * L::kBBytes);
+                const int r = kt % RST;
+                if (kt >= RST && !mt_mbar_wait(&rempty[r], (uint32_t)((kt / RST) - 1) & 1u, abort_flag, status, 1))
+                    break;
+                mt_mbar_expect_tx(&rfull[r], L::kRawBytes);
                 const int kg = (kbeg + kt) * 32;
-                mt_tma_load_2d(A_raw(s), tmA, &full[s], kg, m0);
+                mt_tma_load_2d(A_raw(r), tmA, &rfull[r], kg, m0);
                 for (int b = 0; b < NB; ++b) {
                     const mt_tmap* tb = b == 0 ? tmB0 : tmB1;
-                    if (B_MN) mt_tma_load_3d(B_dst(s, b), tb, &full[s], 0, kg, n0 / 32);
-                    else mt_tma_load_2d(B_dst(s, b), tb, &full[s], kg, n0);
+                    if (B_MN) mt_tma_load_3d(B_raw(r, b), tb, &rfull[r], 0, kg, n0 / 32);
+                    else mt_tma_load_2d(B_raw(r, b), tb, &rfull[r], kg, n0);
                 }
                 issued = kt + 1;
             }
             if (*abort_flag) {  // let this CTA's own copies land before it can exit
-                for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
-                    mt_mbar_drain(&full[kt % STAGES], (uint32_t)(kt / STAGES) & 1u);
+                for (int kt = (issued > RST ? issued - RST : 0); kt < issued; ++kt)
+                    mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = mt_idesc_tf32(128, NB * BN, false, B_MN);
             bool ok = true;
-            for (int c = 0; c < nchunks && ok; ++c) {
-                const int tb = c & 1;
-                if (c >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((c >> 1) - 1) & 1u, abort_flag, status, 2)) break;
+            for (int ch = 0; ch < nchunks && ok; ++ch) {
+                const int tb = ch & 1;
+                if (ch >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch >> 1) - 1) & 1u, abort_flag, status, 2))
+                    break;
                 mt_tc_fence_after();
-                const int kt0 = c * CHUNK, kt1 = min(kt0 + CHUNK, nk);
+                const int kt0 = ch * CHUNK, kt1 = min(kt0 + CHUNK, nk);
                 for (int kt = kt0; kt < kt1; ++kt) {
-                    const int s = kt % STAGES;
-                    if (!mt_mbar_wait(&conv[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 2)) {
+                    const int c = kt % CST;
+                    if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
                         ok = false;
                         break;
                     }
                     mt_tc_fence_after();
-                    const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)s;
+                    const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
+                    const uint32_t bh = mt_smem_u32(B_cv(c, 0, 0)), bl = mt_smem_u32(B_cv(c, 0, 1));
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint32_t dah = ah + 8u * (uint32_t)kk;
                         const uint32_t dal = dah + 32u;
                         const uint32_t d = tmem + (uint32_t)(tb * NB * BN);
-                        const uint64_t dbh = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_hi(s, 0)), kk)
-                                                  : mt_operand_desc_k(mt_smem_u32(B_hi(s, 0)), kk);
-                        const uint64_t dbl = B_MN ? mt_operand_desc_mn(mt_smem_u32(B_lo(s, 0)), kk)
-                                                  : mt_operand_desc_k(mt_smem_u32(B_lo(s, 0)), kk);
+                        const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
+                        const uint64_t dbl = B_MN ? mt_operand_desc_mn(bl, kk) : mt_operand_desc_k(bl, kk);
                         mt_mma_tf32_ts(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
                         mt_mma_tf32_ts(d, dal, dbh, idesc, 1u);
                         mt_mma_tf32_ts(d, dah, dbh, idesc, 1u);
                     }
-                    mt_mma_commit(&empty[s]);
+                    mt_mma_commit(&cempty[c]);
                 }
                 mt_mma_commit(&tfull[tb]);
             }
@@ -646,20 +656,26 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
         const int cw = warp - 2;                    // converter warp 0..5
         const int ct = cw * 32 + lane;              // 0..191
         for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % STAGES;
-            if (!mt_mbar_wait(&full[s], (uint32_t)(kt / STAGES) & 1u, abort_flag, status, 3)) break;
+            const int r = kt % RST, c = kt % CST;
+            if (!mt_mbar_wait(&rfull[r], (uint32_t)(kt / RST) & 1u, abort_flag, status, 3)) break;
+            // the converted stage (B buffers and A's TMEM slot) is free once the MMAs
+            // of k-tile kt - CST completed
+            if (kt >= CST && !mt_mbar_wait(&cempty[c], (uint32_t)((kt / CST) - 1) & 1u, abort_flag, status, 3)) break;
+            mt_tc_fence_after();
             if (warp >= 4)
-                mt_convert_a_rows(A_raw(s), tmem + ACOLS + 64u * (uint32_t)s, warp & 3, lane, m0, (kbeg + kt) * 32, M, K,
-                                  proA);
-            // The split is elementwise, so it runs in place whatever the swizzle; the
-            // prologue (coordinates) is only supported on K-major B tiles.
+                mt_convert_a_rows(A_raw(r), tmem + ACOLS + 64u * (uint32_t)c, warp & 3, lane, m0, (kbeg + kt) * 32, M,
+                                  K, proA);
+            // the prologue (coordinates) is only supported on K-major B tiles
             for (int b = 0; b < NB; ++b)
-                mt_convert_tile<false, false, BN, NCONV * 32>(B_hi(s, b), B_lo(s, b), n0, (kbeg + kt) * 32, N, K, proB,
-                                                              ct);
+                mt_convert_tile<false, false, BN, NCONV * 32>(B_raw(r, b), B_cv(c, b, 0), B_cv(c, b, 1), n0,
+                                                              (kbeg + kt) * 32, N, K, proB, ct);
             mt_fence_proxy_async();
             mt_tc_fence_before();
             __syncwarp();
-            if (lane == 0) mt_mbar_arrive(&conv[s]);
+            if (lane == 0) {
+                mt_mbar_arrive(&rempty[r]);
+                mt_mbar_arrive(&cfull[c]);
+            }
         }
     } else {
         const int q = warp & 3;                     // TMEM lane quarter

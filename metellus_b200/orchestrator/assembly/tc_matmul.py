@@ -92,20 +92,26 @@ def _tmap(buf_index: int, t: Tensor, layout: str, outer_box: int) -> TmapSpec:
     return TmapSpec(buf_index, (32, kdim, rows // 32), (ld * 4, 128), (32, 32, outer_box // 32), swizzle=4)
 
 
-def _stage_bytes(bn: int, nb: int, b_mn: bool) -> int:
-    """A (its hi / lo split lives in tensor memory), then per anchor B hi + B lo
-    (split in place)."""
-    return 128 * 32 * 4 + nb * 2 * bn * 32 * 4
+def _raw_bytes(bn: int, nb: int) -> int:
+    """A raw-ring stage: the TMA targets A and B of every anchor."""
+    return 128 * 32 * 4 + nb * bn * 32 * 4
+
+
+def _conv_bytes(bn: int, nb: int) -> int:
+    """A converted-ring stage: B hi + B lo of every anchor (A's split lives in tensor
+    memory)."""
+    return 2 * nb * bn * 32 * 4
 
 
 def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True, K: int = 0) -> tuple[int, int, int]:
-    """(BN, stages, split-K): the widest N tile that still gives ~one CTA per SM, and
-    as many pipeline stages as fit the shared-memory budget and tensor memory (512
-    columns: two accumulator chunks of nb * BN columns, plus 64 columns of A hi / lo
-    per stage). A k-tile costs about the same time at BN = 64 as at 128 (the A split
-    and the pipeline hand-offs dominate), so an output with too few 128-wide tiles to
-    fill the SMs keeps BN = 128 and splits K over a two-CTA cluster instead of halving
-    BN (C = 1024^3: 64 tiles -> 128 CTAs of 16 k-tiles each)."""
+    """(BN, stages, split-K): the widest N tile that still gives ~one CTA per SM; as
+    many stages (each raw + converted ring gets `stages` entries) as fit the
+    shared-memory budget and tensor memory (512 columns: two accumulator chunks of
+    nb * BN columns, plus 64 columns of A hi / lo per converted stage). A k-tile costs
+    about the same time at BN = 64 as at 128 (the A split and the pipeline hand-offs
+    dominate), so an output with too few 128-wide tiles to fill the SMs keeps BN = 128
+    and splits K over a two-CTA cluster instead of halving BN (C = 1024^3: 64 tiles ->
+    128 CTAs of 16 k-tiles each)."""
     tiles_m = -(-M // 128)
     tiles128 = tiles_m * -(-N // 128)
     splitk = 1
@@ -116,12 +122,12 @@ def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True, K: int = 0) -> tuple[
     else:
         bn = 64
     tmem_stages = (512 - 2 * nb * bn) // 64
-    stages = max(2, min(6, tmem_stages, SMEM_BUDGET // _stage_bytes(bn, nb, b_mn)))
+    stages = max(2, min(4, tmem_stages, SMEM_BUDGET // (_raw_bytes(bn, nb) + _conv_bytes(bn, nb))))
     return bn, stages, splitk
 
 
 def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
-    return stages * _stage_bytes(bn, nb, b_mn) + (3 * stages + 6) * 8 + 16 + 1024
+    return stages * (_raw_bytes(bn, nb) + _conv_bytes(bn, nb)) + (4 * stages + 6) * 8 + 16 + 1024
 
 
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
@@ -194,7 +200,8 @@ class TcGemmFragment:
         lines.append("const mt_epilogue<decltype(epi_f)> epi{epi_f};")
         tb1 = "&tm_b1" if self.nb > 1 else "&tm_b0"
         lines.append(
-            f"mt_gemm_3xtf32<{self.bn}, {self.stages}, {str(self.a_mn).lower()}, {str(self.b_mn).lower()}, "
+            f"mt_gemm_3xtf32<{self.bn}, {self.stages}, {self.stages}, {str(self.a_mn).lower()}, "
+            f"{str(self.b_mn).lower()}, "
             f"{self.nb}, {self.splitk}>(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, "
             "tc_arena);"
         )
