@@ -280,10 +280,13 @@ def assemble_row_resident(decision: DecisionView, function_name: str | None) -> 
     params = tuple(param_decl(k, writable=k in out_keys) for k in bindings)
     frag = RowResidentFragment(ops=ops, outputs=outputs, rows=R, rows_per_batch=Mb, cols=K, width=width,
                                chunks=chunks)
-    blocks_per_sm = max(1, 2048 // nt)
+    # One wave: the grid is exactly the CTAs that are resident at once (threads per
+    # SM 2048, registers capped at ~40 per thread by the launch bounds), each looping
+    # over rows; a grid of 2048 / nt CTAs per SM would leave a partial second wave.
+    blocks_per_sm = max(1, min(2048 // nt, 65536 // (nt * 40)))
     grid = max(1, min(R, SM_COUNT * blocks_per_sm))
     fn = function_name or f"row_{ops[-1].out.name}_fused"
     ctx = CodegenContext(function_name=fn, buffers=params, dims=("R", "K"), tg_x=nt, tg_y=1,
-                         threadgroup_decls=("smem float red_scratch[33];",))
+                         threadgroup_decls=("smem float red_scratch[33];",), min_blocks_per_sm=blocks_per_sm)
     return KernelGroup(kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(R, K),
                        grid=(grid, 1, 1), threads=(nt, 1, 1), ops=ops, strategy=decision.strategy)
