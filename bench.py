@@ -462,7 +462,8 @@ def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
     once, persistent device buffers, kernels replayed from a CUDA graph) called on
     pinned host inputs, writing the output into a pinned host array; each step's
     host-to-device input copies, kernels and device-to-host output copy are inside the
-    CUDA events."""
+    CUDA events (a step's download runs on the copy stream, overlapping the next step's
+    uploads; the closing event waits for the last one)."""
     from metellus_b200 import distributed
     from metellus_b200.api.executable import Executable
     from metellus_b200.runtime import backend
@@ -500,6 +501,7 @@ def run_e2e(ops, groups, key, shape, world, args, dist, barrier) -> dict:
     e0.record()
     for _ in range(steps):
         step()
+    exe.join()  # the last step's download (copy stream) inside the timed region
     e1.record()
     barrier()
     exe.synchronize()

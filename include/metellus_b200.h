@@ -55,6 +55,15 @@ int mt_buffer_read_async(uint64_t handle, void* dst, size_t nbytes);
 int mt_buffer_fill(uint64_t handle, uint8_t value);
 /* Stream-ordered form of mt_buffer_fill: returns without waiting for the device. */
 int mt_buffer_fill_async(uint64_t handle, uint8_t value);
+/* Device-to-host copy on the device's copy stream (not the main stream): waits for
+ * event `after` (recorded on the main stream, e.g. after the kernels that produce the
+ * data; 0 = no wait), then records event `done` (0 = none) when the copy finishes.
+ * A step's download then overlaps the next step's uploads (PCIe is full duplex; the
+ * main stream carries uploads and kernels). No counterpart in the reference (its
+ * read_buffer is synchronous). */
+int mt_buffer_read_after(uint64_t handle, void* dst, size_t nbytes, uint64_t after, uint64_t done);
+/* The device's main stream waits for event `ev` before its next operation. */
+int mt_stream_wait_event(int dev, uint64_t ev);
 /* Pinned host memory for fast host<->device copies. */
 int mt_host_alloc(size_t nbytes, void** ptr);
 int mt_host_free(void* ptr);
@@ -94,7 +103,7 @@ int mt_launch(int dev, uint64_t kernel, const uint64_t* buffers, int nbuf,
               const uint32_t* dims, int ndims, const uint32_t grid[3],
               const uint32_t block[3], uint32_t dyn_smem, uint32_t cluster_x,
               const mt_tmap_spec* tmaps, int ntmaps, float* time_ms);
-/* Wait for all work on the device's stream. */
+/* Wait for all work on the device's streams (main and copy). */
 int mt_sync(int dev);
 
 /* ---- native kernels ------------------------------------------------------- */

@@ -6,7 +6,9 @@ many times on new inputs; ``Executable`` does the planning and compilation once,
 keeps every bound device buffer for its lifetime (a persistent pool for the
 program), and replays the dispatch list from a CUDA graph (captured on the second
 call, after the first call has loaded every module), so a call costs the input
-copies, one graph launch and the output copies::
+copies, one graph launch and the output copies. Downloads run on the device's copy
+stream, after the kernels and overlapping the next call's uploads (PCIe is full
+duplex); the next call's kernels wait for them before overwriting the outputs::
 
     exe = Executable(ops, outputs=("out",))
     res = exe({"x": x, "y": y, "z": z})          # dict name -> host ndarray
@@ -65,6 +67,9 @@ class Executable:
         self._graph_ok = graph and not any("nccl" in (g.pipe or "") for g in self.groups)
         self._graph: int | None = None
         self._calls = 0
+        self._kernels_done = backend.Event()
+        self._read_done = backend.Event()
+        self._read_pending = False
 
     # -- execution ------------------------------------------------------------------
 
@@ -100,24 +105,41 @@ class Executable:
                 raise ValueError(f"Executable: input {name!r} has shape {np.shape(arr)}, "
                                  f"expected {tensors[name].shape}")
             self.env[self.input_keys[name]].write(np.asarray(arr, dtype=np.float32), wait=False)
+        if self._read_pending:  # the previous call's downloads must finish before the outputs change
+            backend.stream_wait_event(self._read_done)
         self._launch()
         self._calls += 1
+        self._kernels_done.record()
         results: dict[str, np.ndarray] = {}
-        for name in self.outputs:
+        for k, name in enumerate(self.outputs):
             t = tensors[name]
             dst = (out or {}).get(name)
             if dst is None:
                 dst = np.empty(t.shape, dtype=np.float32)
             if t.buffer_key != t.name:
                 raise ValueError(f"Executable: output {name!r} is a view; request its owner {t.buffer_key!r}")
-            results[name] = self.env[t.buffer_key].read_into(dst, wait=False)
+            if dst.nbytes > self.env[t.buffer_key].nbytes or not dst.flags["C_CONTIGUOUS"]:
+                raise ValueError(f"Executable: destination for {name!r} is not a contiguous array of its size")
+            last = k == len(self.outputs) - 1
+            backend.read_buffer_after(self.env[t.buffer_key].handle, dst, after=self._kernels_done,
+                                      done=self._read_done if last else None)
+            results[name] = dst
+        self._read_pending = bool(self.outputs)
         if wait:
             self.synchronize()
         return results
 
+    def join(self) -> None:
+        """Order the device's main stream after the pending downloads (no host wait):
+        an event recorded on the main stream afterwards covers them."""
+        if self._read_pending:
+            backend.stream_wait_event(self._read_done)
+
     def synchronize(self) -> None:
-        """Wait for the device, then raise if a kernel's bounded wait timed out."""
+        """Wait for the device (kernels and downloads), then raise if a kernel's bounded
+        wait timed out."""
         backend.sync()
+        self._read_pending = False
         if STATUS_KEY in self.env:
             CheckStatus(STATUS_KEY).execute(self.env)
 

@@ -96,6 +96,7 @@ constexpr int kMaxDev = 16;
 struct Device {
     bool ready = false;
     cudaStream_t stream = nullptr;
+    cudaStream_t d2h = nullptr;  // copy stream for downloads that overlap the next uploads
     cudaMemPool_t pool = nullptr;
     ncclComm_t comm = nullptr;  // set by mt_nccl_init
 };
@@ -129,6 +130,7 @@ int ensure_dev(int dev) {
     if (d.ready) return 0;
     RT_CHECK(cudaFree(nullptr));  // create / bind the primary context
     RT_CHECK(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+    RT_CHECK(cudaStreamCreateWithFlags(&d.d2h, cudaStreamNonBlocking));
     RT_CHECK(cudaDeviceGetDefaultMemPool(&d.pool, dev));
     uint64_t keep = ~0ull;  // keep freed blocks cached in the pool
     RT_CHECK(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
@@ -392,6 +394,33 @@ int mt_buffer_write(uint64_t h, const void* src, size_t n) { return copy_common(
 int mt_buffer_read(uint64_t h, void* dst, size_t n) { return copy_common(h, dst, n, false, true); }
 int mt_buffer_write_async(uint64_t h, const void* src, size_t n) { return copy_common(h, (void*)src, n, true, false); }
 int mt_buffer_read_async(uint64_t h, void* dst, size_t n) { return copy_common(h, dst, n, false, false); }
+
+int mt_buffer_read_after(uint64_t h, void* dst, size_t n, uint64_t after, uint64_t done) {
+    Buffer b;
+    cudaStream_t s;
+    cudaEvent_t ea = nullptr, ed = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (get_buf(h, &b)) return 1;
+        s = g_dev[b.dev].d2h;
+        if (after) {
+            auto it = g_events.find(after);
+            if (it == g_events.end()) return fail("mt_buffer_read_after: unknown event %llu", (unsigned long long)after);
+            ea = it->second;
+        }
+        if (done) {
+            auto it = g_events.find(done);
+            if (it == g_events.end()) return fail("mt_buffer_read_after: unknown event %llu", (unsigned long long)done);
+            ed = it->second;
+        }
+    }
+    if (n > b.size) return fail("copy of %zu bytes exceeds buffer of %zu bytes", n, b.size);
+    RT_CHECK(cudaSetDevice(b.dev));
+    if (ea) RT_CHECK(cudaStreamWaitEvent(s, ea, 0));
+    RT_CHECK(cudaMemcpyAsync(dst, b.ptr, n, cudaMemcpyDeviceToHost, s));
+    if (ed) RT_CHECK(cudaEventRecord(ed, s));
+    return 0;
+}
 
 int mt_buffer_fill(uint64_t handle, uint8_t value) {
     Buffer b;
@@ -821,13 +850,24 @@ int mt_allreduce_f64(int dev, uint64_t buf, uint64_t count, int op, uint64_t out
     return 0;
 }
 
+int mt_stream_wait_event(int dev, uint64_t ev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (ensure_dev(dev)) return 1;
+    auto it = g_events.find(ev);
+    if (it == g_events.end()) return fail("mt_stream_wait_event: unknown event %llu", (unsigned long long)ev);
+    RT_CHECK(cudaStreamWaitEvent(g_dev[dev].stream, it->second, 0));
+    return 0;
+}
+
 int mt_sync(int dev) {
-    cudaStream_t s;
+    cudaStream_t s, s2;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         if (ensure_dev(dev)) return 1;
         s = g_dev[dev].stream;
+        s2 = g_dev[dev].d2h;
     }
+    RT_CHECK(cudaStreamSynchronize(s2));
     RT_CHECK(cudaStreamSynchronize(s));
     RT_CHECK(cudaGetLastError());
     return 0;

@@ -54,7 +54,8 @@ class MtTmapSpec(ctypes.Structure):
 EXPORTED = (
     "mt_last_error", "mt_device_count", "mt_init", "mt_device_attr", "mt_buffer_create",
     "mt_buffer_release", "mt_buffer_size", "mt_buffer_ptr", "mt_buffer_write", "mt_buffer_read",
-    "mt_buffer_write_async", "mt_buffer_read_async", "mt_buffer_fill", "mt_buffer_fill_async", "mt_host_alloc",
+    "mt_buffer_write_async", "mt_buffer_read_async", "mt_buffer_fill", "mt_buffer_fill_async",
+    "mt_buffer_read_after", "mt_stream_wait_event", "mt_host_alloc",
     "mt_host_free", "mt_nvrtc_compile", "mt_kernel_load", "mt_kernel_info", "mt_launch", "mt_sync",
     "mt_event_create", "mt_event_record", "mt_event_elapsed", "mt_event_destroy",
     "mt_graph_begin", "mt_graph_end", "mt_graph_launch", "mt_graph_destroy", "mt_reduce_rows",
@@ -92,6 +93,8 @@ def lib() -> ctypes.CDLL:
                 "mt_buffer_read_async": [u64, ctypes.c_void_p, sz],
                 "mt_buffer_fill": [u64, ctypes.c_uint8],
                 "mt_buffer_fill_async": [u64, ctypes.c_uint8],
+                "mt_buffer_read_after": [u64, ctypes.c_void_p, sz, u64, u64],
+                "mt_stream_wait_event": [i32, u64],
                 "mt_host_alloc": [sz, P(ctypes.c_void_p)],
                 "mt_host_free": [ctypes.c_void_p],
                 "mt_nvrtc_compile": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_void_p, sz,
@@ -206,6 +209,19 @@ def read_buffer(handle: int, out: np.ndarray, *, wait: bool = True) -> None:
         raise ValueError("read_buffer: destination must be C-contiguous")
     fn = lib().mt_buffer_read if wait else lib().mt_buffer_read_async
     _check(fn(handle, out.ctypes.data, out.nbytes))
+
+
+def read_buffer_after(handle: int, out: np.ndarray, after: "Event | None" = None,
+                      done: "Event | None" = None) -> None:
+    """Device-to-host copy on the copy stream after event ``after``; records ``done``."""
+    if not out.flags["C_CONTIGUOUS"]:
+        raise ValueError("read_buffer_after: destination must be C-contiguous")
+    _check(lib().mt_buffer_read_after(handle, out.ctypes.data, out.nbytes, after.handle if after else 0,
+                                      done.handle if done else 0))
+
+
+def stream_wait_event(ev: "Event", dev: int | None = None) -> None:
+    _check(lib().mt_stream_wait_event(_device if dev is None else dev, ev.handle))
 
 
 def fill_buffer(handle: int, value: int, *, wait: bool = True) -> None:
