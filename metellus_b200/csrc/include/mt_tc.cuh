@@ -2,7 +2,7 @@
 // mainloop used by every tcgen05 matmul group (standalone, with prologue / epilogue,
 // and the two-anchor diamond).
 //
-// 3xTF32: each fp32 operand x is split as hi = round_tf32(x), lo = x - hi
+// 3xTF32: each fp32 operand x is split as hi = x rounded to tf32, lo = x - hi
 // and the product is accumulated in fp32 TMEM as hi*hi + hi*lo + lo*hi, which keeps
 // about 22 bits of each operand (fp32 carries 24): normwise error close to an fp32
 // dot product, at tensor-core rate.
@@ -317,16 +317,13 @@ __device__ __forceinline__ void mt_split_tf32(float x, float& hi, float& lo) {
 // warp roles are listed at mt_gemm_3xtf32.
 //
 // Operand tiles in shared memory, per stage:
-//   A K-major  : TMA box {32 (k), 128 (m)}, rows of 128 B, 8-row atoms (SBO 1024 B),
-//                MMA k-step of 8 = +32 B.
-//   A MN-major : TMA 3-D box {32 (m), 32 (k), 4 (m/32)}: 32-column chunks of 4 KB
-//                (LBO 4096 B), k rows of 128 B (SBO 1024 B), MMA k-step = +1024 B.
-//   B likewise with n in place of m.
+//   A          : TMA box {32 (k), 128 (m)}, K-major, rows of 128 B, 8-row atoms
+//                (SBO 1024 B); split into tensor memory, where the MMA reads it.
+//   B K-major  : TMA box {32 (k), BN (n)}, as A; MMA k-step of 8 = +32 B.
+//   B MN-major : TMA 3-D box {32 (n), 32 (k), BN/32}: 32-column chunks of 4 KB
+//                (LBO 4096 B), k rows of 128 B in 4-row swizzle atoms (SBO 512 B),
+//                MMA k-step = +1024 B.
 // ---------------------------------------------------------------------------------
-
-struct mt_gemm_smem_plan {
-    static constexpr uint32_t kBK = 32;
-};
 
 template <int BN, int RSTAGES, int CSTAGES, bool A_MN, bool B_MN, int NB>
 struct mt_gemm_layout {
@@ -389,8 +386,8 @@ struct mt_no_prologue {
     __device__ __forceinline__ float operator()(float x, int, int) const { return x; }
 };
 
-// Split one landed fp32 tile in place: hi overwrites the tile, lo goes to `lo`.
-// `rows` is the tile extent along M (A) or N (B); `r0` / `k0` its global origin;
+// Split one landed fp32 tile: hi to `hi` (the tile itself for an in-place split), lo
+// to `lo`. `ROWS` is the tile extent along M (A) or N (B); `r0` / `k0` its global origin;
 // `rlim` / `klim` the global bounds (prologue transforms only touch in-bounds
 // elements; out-of-bounds elements were zero-filled by TMA and stay 0).
 // Convert one landed tile in two phases so every shared-memory load of the thread is
