@@ -6,6 +6,9 @@ from __future__ import annotations
 
 from metellus_b200.compute.fragments import CodegenContext
 from metellus_b200.compute.reduction import (
+    COLRED_COLS,
+    COLRED_WARPS,
+    ColumnReductionFragment,
     LastAxisReductionComputeFragment,
     LastAxisReductionSetupFragment,
     StoreReductionResultFragment,
@@ -78,12 +81,63 @@ def _combined_reduction(decision: DecisionView, function_name: str | None, src, 
                        pipe="native+nccl", scratch=((PARTIAL_KEY, 8 * M),))
 
 
+COLRED_TARGET_BLOCKS = 148 * 8   # ~8 resident 256-thread blocks per SM
+COLRED_MIN_CHUNK = 64            # reduced indices per split (8 per warp)
+
+
+def column_reduction_plan(M: int, K: int) -> tuple[int, int]:
+    """(column blocks, splits of the reduced axis) for an M-output, K-deep column
+    reduction: enough blocks to fill the GPU, each split at least 64 indices deep."""
+    colblocks = -(-M // COLRED_COLS)
+    want = -(-COLRED_TARGET_BLOCKS // colblocks)
+    splits = max(1, min(want, K // COLRED_MIN_CHUNK, 65535))
+    return colblocks, splits
+
+
+def assemble_column_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup | None:
+    """A reduction over a view with contiguous rows (``reduction(transpose(X))``):
+    the coalesced column kernel (``ColumnReductionFragment``) with the prologue chain
+    applied to each load and the epilogue chain to each result. None when the view
+    is not of that layout."""
+    anchor = decision.anchor
+    src = decision.prologue_a[0].operands[0] if decision.prologue_a else anchor.input
+    if not isinstance(src, Tensor) or len(src.shape) != 2 or src.row_stride != 1 or src.col_stride == 1:
+        return None
+    M, K = src.shape
+    final_out = decision.epilogue[-1].out if decision.epilogue else anchor.out
+    colblocks, splits = column_reduction_plan(M, K)
+    part_key, ticket_key = f"__mt_colpart_{anchor.out.name}", f"__mt_colticket_{anchor.out.name}"
+    scratch = ((part_key, 4 * splits * M), (ticket_key, 4 * colblocks)) if splits > 1 else ()
+    extras = Extras(base_slots_by_key={src.buffer_key: 0, final_out.buffer_key: 1})
+    pro = chain_value_transform(decision.prologue_a, row_var="row", col_var="idx", extras=extras,
+                                base_slot=2) if decision.prologue_a else None
+    epi = build_reduction_epilogue_transform(decision.epilogue) if decision.epilogue else None
+    vec = M % 4 == 0 and src.col_stride % 4 == 0
+    frag = ColumnReductionFragment(op=anchor.op, input_name=pname(src.buffer_key),
+                                   output_name=pname(final_out.buffer_key), part_name=pname(part_key),
+                                   ticket_name=pname(ticket_key), col_stride=src.col_stride, splits=splits,
+                                   vec=vec, name="column_reduction", value_transform=pro, epilogue=epi)
+    # parameter order = dispatch order: bindings (input, output, extras) then scratch
+    params = (param_decl(src.buffer_key), param_decl(final_out.buffer_key, writable=True), *extras.buffers,
+              *(param_decl(k, writable=True) for k, _ in scratch))
+    fn = function_name or f"reduce_cols_{anchor.out.name}"
+    ctx = CodegenContext(function_name=fn, buffers=params, dims=("M", "K"), tg_x=COLRED_WARPS * 32, tg_y=1,
+                         threadgroup_decls=(f"smem float colred_sh[{COLRED_WARPS}][{COLRED_COLS}];",))
+    return KernelGroup(kernel=Kernel(fragments=(frag,), ctx=ctx),
+                       bindings=(src.buffer_key, final_out.buffer_key, *extras.bindings), dims=(M, K),
+                       grid=(colblocks, splits, 1), threads=(COLRED_WARPS * 32, 1, 1), ops=decision.ops,
+                       strategy=decision.strategy, scratch=scratch)
+
+
 def assemble_reduction(decision: DecisionView, function_name: str | None) -> KernelGroup:
     anchor = decision.anchor
     assert isinstance(anchor, ReductionOp)
     split = assemble_split_reduction(decision, function_name)
     if split is not None:
         return split
+    col = assemble_column_reduction(decision, function_name)
+    if col is not None:
+        return col
     src = decision.prologue_a[0].operands[0] if decision.prologue_a else anchor.input
     assert isinstance(src, Tensor)
     M, K = src.matrix_shape
