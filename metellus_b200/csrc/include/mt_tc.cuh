@@ -128,6 +128,15 @@ __device__ __forceinline__ bool mt_mbar_wait_cluster(uint64_t* bar, uint32_t par
         }
     }
 }
+// Arrive on an mbarrier in another cluster CTA's shared memory with the default
+// release at CTA scope: no cluster-scope fence (a release.cluster arrive stalls the
+// warp on a memory barrier). For hand-offs that publish no generic-proxy data to
+// the other CTA: tensor-memory reads done (tcgen05.wait::ld), or operands this CTA
+// wrote into its own shared memory for the pair's MMAs, made visible to the async
+// proxy by fence.proxy.async first.
+__device__ __forceinline__ void mt_mbar_arrive_peer(uint32_t remote_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(remote_bar) : "memory");
+}
 // Cluster-wide barrier: every thread of both CTAs executes it right after set-up
 // (mbarrier initialisation), before any role can wait on anything.
 __device__ __forceinline__ void mt_cluster_sync() {
@@ -218,6 +227,43 @@ __device__ __forceinline__ void mt_mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  :: "r"(mt_smem_u32(bar)) : "memory");
 }
+// ---- CTA-pair (cta_group::2) forms, used by mt_gemm_3xtf32_pair. A kernel uses
+// either these or the one-CTA forms above for all of its tcgen05 instructions.
+
+// One warp in each CTA of the pair: the same columns are allocated in both CTAs'
+// tensor memory and each CTA's slot receives the address.
+__device__ __forceinline__ void mt_tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(mt_smem_u32(slot)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mt_tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A * B over the pair, issued by one thread of the even CTA: M = 256, rows
+// [0, 128) from the even CTA and [128, 256) from the odd one; A from each CTA's
+// tensor memory at `a_tmem`, B's N columns split in halves between the two CTAs'
+// shared memory at the descriptor's address; each CTA's D holds its 128 rows.
+__device__ __forceinline__ void mt_mma_tf32_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                    uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive on the mbarrier at `bar`'s offset in both CTAs of the pair once this
+// thread's earlier pair MMAs complete.
+__device__ __forceinline__ void mt_mma_commit_pair_both(uint64_t* bar) {
+    const unsigned short both = 3;
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 :: "r"(mt_smem_u32(bar)), "h"(both) : "memory");
+}
+// The same for this CTA's barrier only.
+__device__ __forceinline__ void mt_mma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(mt_smem_u32(bar)) : "memory");
+}
+
 // 32 lanes x 32 consecutive fp32 columns: thread t of the warp gets lane (base+t).
 __device__ __forceinline__ void mt_tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
@@ -753,5 +799,237 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     if (warp == 1) {
         mt_tc_fence_after();
         mt_tmem_dealloc(tmem, NCOLS);
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// CTA-pair GEMM: a 256 x 128 output tile per cluster of two CTAs (cta_group::2).
+//
+// The even CTA (rank 0) issues every MMA for both: M = 256 (its 128 A rows and the
+// odd CTA's 128, each from its own tensor memory) x N = 128, with B's 128 columns
+// split between the two CTAs' shared memory (64 each). Per CTA and k-tile this moves
+// half of the B bytes of the one-CTA 128 x 128 tile through TMA, the converters and
+// the MMA operand reads, for the same MMA work per SM: shared-memory traffic per
+// k-tile drops from ~144 KB to ~88 KB, below what the MMAs need in issue time.
+//
+// Columns: one anchor (NB = 1, BN = 128): rank r holds B columns [n0 + 64r, +64).
+// Two anchors sharing A (NB = 2, BN = 64): rank b holds anchor b's 64 columns, so D
+// columns [0, 64) are anchor 0 and [64, 128) anchor 1, as in the one-CTA layout.
+//
+// Same warp roles as mt_gemm_3xtf32 in each CTA. Hand-offs across the pair: the odd
+// CTA's converters arrive on the even CTA's cfull (remote arrive, release at CTA
+// scope, after the proxy and tcgen05 fences), its accumulator warps on the even
+// CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
+// (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
+// before tensor memory is freed and either exits.
+template <int BN, int RST, int CST, bool B_MN, int NB, class ProA, class ProB, class Epi>
+__device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
+                                                    int M, int N, int K, const ProA& proA, const ProB& proB,
+                                                    const Epi& epi, int* status, void* smem_raw) {
+    constexpr int NMMA = NB * BN;                 // MMA N: 128
+    constexpr int BROWS = NMMA / 2;               // B rows (n) per CTA and stage: 64
+    constexpr int HALF = BN / 2;                  // columns per accumulator warp per anchor
+    constexpr uint32_t kABytes = 128u * 32u * 4u;
+    constexpr uint32_t kBBytes = (uint32_t)BROWS * 32u * 4u;
+    constexpr uint32_t kRawBytes = kABytes + kBBytes;
+    constexpr uint32_t kConvBytes = 2u * kBBytes;
+    constexpr uint32_t kConvOffset = RST * kRawBytes;
+    constexpr uint32_t kBarOffset = kConvOffset + CST * kConvBytes;
+    constexpr uint32_t ACOLS = 2u * NMMA;         // two chunk buffers of accumulators
+    static_assert(NMMA == 128, "pair tiles are 256 x 128");
+    static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
+    static_assert(ACOLS + 64u * CST <= 512, "accumulators and A stages exceed TMEM");
+    constexpr uint32_t NCOLS = 512;
+    constexpr int NCONV = 6;
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* rfull = reinterpret_cast<uint64_t*>(smem + kBarOffset);
+    uint64_t* rempty = rfull + RST;
+    uint64_t* cfull = rempty + RST;     // used on rank 0: both CTAs' converters
+    uint64_t* cempty = cfull + CST;     // both CTAs: rank 0's MMA commit
+    uint64_t* tfull = cempty + CST;     // [2] both CTAs: rank 0's MMA commit
+    uint64_t* tempty = tfull + 2;       // [2] used on rank 0: both CTAs' accumulator warps
+    uint64_t* mdone = tempty + 2;       // rank 0: MMAs drained on the abort path
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+    const int rank = (int)mt_cluster_rank();
+    int m0, n0;
+    {
+        constexpr int kGroupM = 8;              // in 256-row pair tiles
+        const int n_tiles = (int)gridDim.x / 2, m_tiles = (int)gridDim.y;
+        const int id = (int)(blockIdx.y * n_tiles + blockIdx.x / 2);
+        const int group = id / (kGroupM * n_tiles);
+        const int first_m = group * kGroupM;
+        const int gsize = min(m_tiles - first_m, kGroupM);
+        const int in_group = id - group * kGroupM * n_tiles;
+        m0 = (first_m + in_group % gsize) * 256 + rank * 128;
+        n0 = (in_group / gsize) * BN;
+    }
+    const int nb0 = NB == 1 ? n0 + rank * BROWS : n0;   // first B column this CTA loads
+    const mt_tmap* tmB = (NB > 1 && rank == 1) ? tmB1 : tmB0;
+    const int nk = (K + 31) / 32;
+    auto A_raw = [&](int r) { return reinterpret_cast<float*>(smem + r * kRawBytes); };
+    auto B_raw = [&](int r) { return reinterpret_cast<float*>(smem + r * kRawBytes + kABytes); };
+    auto B_cv = [&](int c, int j) { return reinterpret_cast<float*>(smem + kConvOffset + c * kConvBytes + j * kBBytes); };
+
+    if (threadIdx.x == 0) {
+        for (int r = 0; r < RST; ++r) {
+            mt_mbar_init(&rfull[r], 1);
+            mt_mbar_init(&rempty[r], NCONV);
+        }
+        for (int c = 0; c < CST; ++c) {
+            mt_mbar_init(&cfull[c], 2 * NCONV);
+            mt_mbar_init(&cempty[c], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mt_mbar_init(&tfull[b], 1);
+            mt_mbar_init(&tempty[b], 16);
+        }
+        mt_mbar_init(mdone, 1);
+        *abort_flag = 0;
+        mt_fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        mt_tma_prefetch(tmA);
+        mt_tma_prefetch(tmB);
+    }
+    if (warp == 1) mt_tmem_alloc_pair(tmem_slot, NCOLS);
+    mt_tc_fence_before();
+    __syncthreads();
+    mt_cluster_sync();  // both CTAs' barriers initialised and tensor memory allocated
+    mt_tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < nk; ++kt) {
+                const int r = kt % RST;
+                if (kt >= RST && !mt_mbar_wait(&rempty[r], (uint32_t)((kt / RST) - 1) & 1u, abort_flag, status, 1))
+                    break;
+                mt_mbar_expect_tx(&rfull[r], kRawBytes);
+                const int kg = kt * 32;
+                mt_tma_load_2d(A_raw(r), tmA, &rfull[r], kg, m0);
+                if (B_MN) mt_tma_load_3d(B_raw(r), tmB, &rfull[r], 0, kg, nb0 / 32);
+                else mt_tma_load_2d(B_raw(r), tmB, &rfull[r], kg, nb0);
+                issued = kt + 1;
+            }
+            if (*abort_flag) {
+                for (int kt = (issued > RST ? issued - RST : 0); kt < issued; ++kt)
+                    mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t idesc = mt_idesc_tf32(256, NMMA, false, B_MN);
+            bool ok = true;
+            int nchunks = nk;
+            for (int ch = 0; ch < nchunks && ok; ++ch) {
+                const int tb = ch & 1;
+                if (ch >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch >> 1) - 1) & 1u, abort_flag, status, 2)) {
+                    ok = false;
+                    break;
+                }
+                mt_tc_fence_after();
+                const int kt = ch, c = kt % CST;
+                if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
+                    ok = false;
+                    break;
+                }
+                mt_tc_fence_after();
+                const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
+                const uint32_t bh = mt_smem_u32(B_cv(c, 0)), bl = mt_smem_u32(B_cv(c, 1));
+                const uint32_t d = tmem + (uint32_t)(tb * NMMA);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t dah = ah + 8u * (uint32_t)kk;
+                    const uint32_t dal = dah + 32u;
+                    const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
+                    const uint64_t dbl = B_MN ? mt_operand_desc_mn(bl, kk) : mt_operand_desc_k(bl, kk);
+                    mt_mma_tf32_ts_pair(d, dah, dbl, idesc, kk ? 1u : 0u);
+                    mt_mma_tf32_ts_pair(d, dal, dbh, idesc, 1u);
+                    mt_mma_tf32_ts_pair(d, dah, dbh, idesc, 1u);
+                }
+                mt_mma_commit_pair_both(&cempty[c]);
+                mt_mma_commit_pair_both(&tfull[tb]);
+            }
+            if (!ok) {  // let the MMAs in flight finish before tensor memory is freed
+                mt_mma_commit_pair_local(mdone);
+                mt_mbar_drain(mdone, 0);
+            }
+        }
+    } else if (warp < 8) {
+        const int cw = warp - 2;
+        const int ct = cw * 32 + lane;
+        const uint32_t cfull_r0 = mt_cluster_map(cfull, 0);
+        for (int kt = 0; kt < nk; ++kt) {
+            const int r = kt % RST, c = kt % CST;
+            if (!mt_mbar_wait(&rfull[r], (uint32_t)(kt / RST) & 1u, abort_flag, status, 3)) break;
+            if (kt >= CST && !mt_mbar_wait(&cempty[c], (uint32_t)((kt / CST) - 1) & 1u, abort_flag, status, 3)) break;
+            mt_tc_fence_after();
+            if (warp >= 4)
+                mt_convert_a_rows(A_raw(r), tmem + ACOLS + 64u * (uint32_t)c, warp & 3, lane, m0, kt * 32, M, K, proA);
+            mt_convert_tile<false, false, BROWS, NCONV * 32>(B_raw(r), B_cv(c, 0), B_cv(c, 1), nb0, kt * 32, N, K,
+                                                             proB, ct);
+            mt_fence_proxy_async();
+            mt_tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mt_mbar_arrive(&rempty[r]);
+                mt_mbar_arrive_peer(cfull_r0 + (uint32_t)(c * 8));
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const int h = (warp - 8) >> 2;
+        const uint32_t tempty_r0 = mt_cluster_map(tempty, 0);
+        float acc[NB][HALF];
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+#pragma unroll
+            for (int j = 0; j < HALF; ++j) acc[b][j] = 0.0f;
+        bool ok = true;
+        for (int c = 0; c < nk; ++c) {
+            const int tb = c & 1;
+            if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c >> 1) & 1u, abort_flag, status, 5)) {
+                ok = false;
+                break;
+            }
+            mt_tc_fence_after();
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+#pragma unroll
+                for (int j = 0; j < HALF / 32; ++j) {
+                    float v[32];
+                    mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * 32), v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[b][j * 32 + i] = __fadd_rn(acc[b][j * 32 + i], v[i]);
+                }
+            }
+            mt_tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mt_mbar_arrive_peer(tempty_r0 + (uint32_t)(tb * 8));
+        }
+        if (ok) {
+            const int row = m0 + q * 32 + lane;
+#pragma unroll
+            for (int j = 0; j < HALF / 32; ++j) {
+                float v[NB][32];
+#pragma unroll
+                for (int b = 0; b < NB; ++b)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[b][i] = acc[b][j * 32 + i];
+                epi.store(row, n0 + h * HALF + j * 32, v);
+            }
+        }
+    }
+    mt_tc_fence_before();
+    __syncthreads();
+    mt_cluster_sync();  // no CTA frees tensor memory or exits while its partner may still use it
+    if (warp == 1) {
+        mt_tc_fence_after();
+        mt_tmem_dealloc_pair(tmem, NCOLS);
     }
 }

@@ -130,6 +130,34 @@ def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
     return stages * (_raw_bytes(bn, nb) + _conv_bytes(bn, nb)) + (4 * stages + 6) * 8 + 16 + 1024
 
 
+# CTA-pair (cta_group::2) tiles: 256 x 128 per two-CTA cluster, 64 B rows per CTA.
+PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
+PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
+PAIR_CSTAGES = 4                                # tensor memory: 256 accumulator columns + 4 x 64 for A
+
+
+def pair_enabled() -> bool:
+    return os.environ.get("METELLUS_TC_PAIR", "1") != "0"
+
+
+def _pick_pair(M: int, N: int, nb: int) -> tuple[int, int, int] | None:
+    """(BN, raw stages, converted stages) of a CTA-pair tile, or None when the output
+    has too few 256 x 128 pair tiles to fill the SMs (about one pair per two SMs)."""
+    if not pair_enabled():
+        return None
+    bn = 128 // nb
+    pairs = -(-M // 256) * -(-N // bn)
+    if pairs < 0.8 * SM_COUNT / 2:
+        return None
+    cst = PAIR_CSTAGES
+    rst = max(2, min(6, (SMEM_BUDGET - cst * PAIR_CONV_BYTES) // PAIR_RAW_BYTES))
+    return bn, rst, cst
+
+
+def _pair_smem_bytes(rst: int, cst: int) -> int:
+    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 5) * 8 + 16 + 1024
+
+
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
     p = pname(t.buffer_key)
     rs, cs = t.row_stride, t.col_stride
@@ -180,12 +208,19 @@ class TcGemmFragment:
     pro_b: str | None
     epi_body: str               # body of the per-(row, 32 columns) store lambda
     splitk: int = 1             # 2: two-CTA cluster per tile, K halves combined via DSMEM
+    pair: tuple[int, int] | None = None  # (raw, converted) stages of a CTA-pair tile
     name: str = "tc_gemm"
     kind: str = "compute"
 
     @property
+    def arena_bytes(self) -> int:
+        if self.pair is not None:
+            return _pair_smem_bytes(*self.pair)
+        return _smem_bytes(self.bn, self.stages, self.nb, self.b_mn)
+
+    @property
     def tgmem_accesses(self) -> tuple[TgmemAccess, ...]:
-        n = _smem_bytes(self.bn, self.stages, self.nb, self.b_mn) // 4
+        n = self.arena_bytes // 4
         return (TgmemAccess("tc_arena", "readwrite", n, (1, n)),)
 
     def render(self, ctx: CodegenContext) -> str:
@@ -199,6 +234,12 @@ class TcGemmFragment:
         lines.append(f"auto epi_f = [=](int row, int col0, float (&v)[{self.nb}][32]) {{\n{self.epi_body}\n}};")
         lines.append("const mt_epilogue<decltype(epi_f)> epi{epi_f};")
         tb1 = "&tm_b1" if self.nb > 1 else "&tm_b0"
+        if self.pair is not None:
+            rst, cst = self.pair
+            lines.append(
+                f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}>"
+                f"(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);")
+            return "\n".join(lines)
         lines.append(
             f"mt_gemm_3xtf32<{self.bn}, {self.stages}, {self.stages}, {str(self.a_mn).lower()}, "
             f"{str(self.b_mn).lower()}, "
@@ -290,6 +331,9 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
             if o.name not in {e.out.name for e in decision.epilogue} and o.name != anchor.out.name:
                 extras.add_tensor(o, base)
     bn, stages, splitk = _pick_tile(M, N, 1, lb == "mn", K)
+    pair = _pick_pair(M, N, 1)
+    if pair is not None:
+        bn, splitk = pair[0], 1
     need_col_check = N % 32 != 0
     epi = _epi_function(decision.epilogue, {anchor.out.name: "v[0][J]"}, out_key,
                         final_out.name, N, N, need_col_check)
@@ -297,11 +341,11 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
     tmaps = (
         _tmap(bindings.index(src_a.buffer_key), src_a, la, 128),
-        _tmap(bindings.index(src_b.buffer_key), src_b, lb, bn),
+        _tmap(bindings.index(src_b.buffer_key), src_b, lb, 64 if pair else bn),
     )
     frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=1, pro_a=pro_a,
-                          pro_b=pro_b, epi_body=epi, splitk=splitk)
-    n_arena = _smem_bytes(bn, stages, 1, lb == "mn") // 4
+                          pro_b=pro_b, epi_body=epi, splitk=splitk, pair=pair[1:] if pair else None)
+    n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
     ctx = CodegenContext(
         function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
@@ -312,9 +356,10 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     )
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
-        grid=(splitk * -(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
+        grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (splitk * -(-N // bn), -(-M // 128), 1),
+        threads=(512, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
-        cluster_x=splitk,
+        cluster_x=2 if pair else splitk,
     )
 
 
@@ -361,18 +406,21 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
             if o.name not in inside:
                 extras.add_tensor(o, out_slot + 1)
     bn, stages, _ = _pick_tile(M, N, 2, lb == "mn", K)
+    pair = _pick_pair(M, N, 2)
+    if pair is not None:
+        bn = pair[0]
     epi = _epi_function(tuple(epi_ops), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key,
                         merge.out.name, N, N, N % 32 != 0)
     bindings = (*in_keys, out_key, *extras.bindings)
     params = tuple(param_decl(k, writable=(k == out_key)) for k in bindings) + ("int* g_status",)
     tmaps = (
         _tmap(bindings.index(a0.a.buffer_key), a0.a, la, 128),
-        _tmap(bindings.index(a0.b.buffer_key), a0.b, lb, bn),
-        _tmap(bindings.index(a1.b.buffer_key), a1.b, lb, bn),
+        _tmap(bindings.index(a0.b.buffer_key), a0.b, lb, 64 if pair else bn),
+        _tmap(bindings.index(a1.b.buffer_key), a1.b, lb, 64 if pair else bn),
     )
     frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=2, pro_a=None, pro_b=None,
-                          epi_body=epi)
-    n_arena = _smem_bytes(bn, stages, 2, lb == "mn") // 4
+                          epi_body=epi, pair=pair[1:] if pair else None)
+    n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_diamond_{merge.out.name}_fused"
     ctx = CodegenContext(
         function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
@@ -384,6 +432,8 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     )
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
-        grid=(-(-N // bn), -(-M // 128), 1), threads=(512, 1, 1), ops=decision.ops,
+        grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (-(-N // bn), -(-M // 128), 1),
+        threads=(512, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
+        cluster_x=2 if pair else 1,
     )

@@ -150,3 +150,37 @@ def test_tc_matmul_split_k_pairs(cuda_device, M, K, N):
     r64 = evaluate(ops, np.float64)
     r32 = evaluate(ops, np.float32)
     assert_matmul_close(res.env[out], r64[out], r32[out], what=f"split-K {M}x{K}x{N}")
+
+
+PAIR_CASES = [
+    dict(M=2048, K=512, N=2048, bias=True, relu=True),
+    dict(M=2100, K=300, N=2016),                    # ragged; the last pair's odd CTA is wholly past M
+    dict(M=2048, K=256, N=1000, transpose_b=True),  # K-major B, ragged N
+    dict(M=1536, K=384, N=2560, prologue=True),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_CASES, ids=lambda c: "x".join(str(c[k]) for k in "MKN") + "".join(
+    k[0] for k, v in c.items() if v is True))
+def test_tc_matmul_cta_pairs(cuda_device, case):
+    """Many output tiles: 256 x 128 tiles on CTA pairs (cta_group::2 MMAs issued by the
+    even CTA, B split between the two CTAs' shared memory)."""
+    ops, out = _mm(**case, seed=case["M"] + case["N"])
+    res = run(ops)
+    g = res.groups[0]
+    assert g.pipe == "tcgen05" and g.cluster_x == 2 and g.grid[1] == -(-case["M"] // 256), (g.pipe, g.grid)
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env[out], r64[out], r32[out], what=f"pair {case}")
+
+
+@pytest.mark.parametrize("M,K,N,tb", [(2048, 256, 1024, False), (1800, 200, 1088, True)])
+def test_dual_gemm_cta_pairs(cuda_device, M, K, N, tb):
+    """The dual GEMM on CTA pairs: the even CTA holds W1's tile, the odd W3's."""
+    ops = _gated(M, K, N, transpose_b=tb, seed=M + N)
+    res = run(ops)
+    g = res.groups[0]
+    assert g.strategy.value == "dual_gemm_epilogue" and g.cluster_x == 2 and g.grid[1] == -(-M // 256)
+    r64 = evaluate(ops, np.float64)
+    r32 = evaluate(ops, np.float32)
+    assert_matmul_close(res.env["U"], r64["U"], r32["U"], what=f"dual pair {M}x{K}x{N} tb={tb}")
