@@ -822,7 +822,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
 // (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
 // before tensor memory is freed and either exits.
-template <int BN, int RST, int CST, bool B_MN, int NB, class ProA, class ProB, class Epi>
+template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, class ProA, class ProB, class Epi>
 __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                     int M, int N, int K, const ProA& proA, const ProB& proB,
                                                     const Epi& epi, int* status, void* smem_raw) {
@@ -925,7 +925,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         if (rank == 0 && lane == 0) {
             constexpr uint32_t idesc = mt_idesc_tf32(256, NMMA, false, B_MN);
             bool ok = true;
-            int nchunks = nk;
+            const int nchunks = (nk + CHUNK - 1) / CHUNK;
             for (int ch = 0; ch < nchunks && ok; ++ch) {
                 const int tb = ch & 1;
                 if (ch >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch >> 1) - 1) & 1u, abort_flag, status, 2)) {
@@ -933,27 +933,30 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                     break;
                 }
                 mt_tc_fence_after();
-                const int kt = ch, c = kt % CST;
-                if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
-                    ok = false;
-                    break;
-                }
-                mt_tc_fence_after();
-                const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
-                const uint32_t bh = mt_smem_u32(B_cv(c, 0)), bl = mt_smem_u32(B_cv(c, 1));
+                const int kt0 = ch * CHUNK, kt1 = min(kt0 + CHUNK, nk);
                 const uint32_t d = tmem + (uint32_t)(tb * NMMA);
+                for (int kt = kt0; kt < kt1; ++kt) {
+                    const int c = kt % CST;
+                    if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    mt_tc_fence_after();
+                    const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
+                    const uint32_t bh = mt_smem_u32(B_cv(c, 0)), bl = mt_smem_u32(B_cv(c, 1));
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t dah = ah + 8u * (uint32_t)kk;
-                    const uint32_t dal = dah + 32u;
-                    const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
-                    const uint64_t dbl = B_MN ? mt_operand_desc_mn(bl, kk) : mt_operand_desc_k(bl, kk);
-                    mt_mma_tf32_ts_pair(d, dah, dbl, idesc, kk ? 1u : 0u);
-                    mt_mma_tf32_ts_pair(d, dal, dbh, idesc, 1u);
-                    mt_mma_tf32_ts_pair(d, dah, dbh, idesc, 1u);
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t dah = ah + 8u * (uint32_t)kk;
+                        const uint32_t dal = dah + 32u;
+                        const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
+                        const uint64_t dbl = B_MN ? mt_operand_desc_mn(bl, kk) : mt_operand_desc_k(bl, kk);
+                        mt_mma_tf32_ts_pair(d, dah, dbl, idesc, (kt != kt0 || kk) ? 1u : 0u);
+                        mt_mma_tf32_ts_pair(d, dal, dbh, idesc, 1u);
+                        mt_mma_tf32_ts_pair(d, dah, dbh, idesc, 1u);
+                    }
+                    mt_mma_commit_pair_both(&cempty[c]);
                 }
-                mt_mma_commit_pair_both(&cempty[c]);
-                mt_mma_commit_pair_both(&tfull[tb]);
+                if (ok) mt_mma_commit_pair_both(&tfull[tb]);
             }
             if (!ok) {  // let the MMAs in flight finish before tensor memory is freed
                 mt_mma_commit_pair_local(mdone);
@@ -971,8 +974,14 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             mt_tc_fence_after();
             if (warp >= 4)
                 mt_convert_a_rows(A_raw(r), tmem + ACOLS + 64u * (uint32_t)c, warp & 3, lane, m0, kt * 32, M, K, proA);
-            mt_convert_tile<false, false, BROWS, NCONV * 32>(B_raw(r), B_cv(c, 0), B_cv(c, 1), nb0, kt * 32, N, K,
-                                                             proB, ct);
+            // BAL: warps 2-3 split B (32 elements per thread, as many as an A row) while
+            // warps 4-7 split A; otherwise all six share B after their A rows
+            if (!BAL)
+                mt_convert_tile<false, false, BROWS, NCONV * 32>(B_raw(r), B_cv(c, 0), B_cv(c, 1), nb0, kt * 32, N, K,
+                                                                 proB, ct);
+            else if (warp < 4)
+                mt_convert_tile<false, false, BROWS, 64>(B_raw(r), B_cv(c, 0), B_cv(c, 1), nb0, kt * 32, N, K, proB,
+                                                         ct);
             mt_fence_proxy_async();
             mt_tc_fence_before();
             __syncwarp();
@@ -991,7 +1000,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
 #pragma unroll
             for (int j = 0; j < HALF; ++j) acc[b][j] = 0.0f;
         bool ok = true;
-        for (int c = 0; c < nk; ++c) {
+        const int nchunks = (nk + CHUNK - 1) / CHUNK;
+        for (int c = 0; c < nchunks; ++c) {
             const int tb = c & 1;
             if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c >> 1) & 1u, abort_flag, status, 5)) {
                 ok = false;
