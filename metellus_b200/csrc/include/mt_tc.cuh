@@ -822,7 +822,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
 // (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
 // before tensor memory is freed and either exits.
-template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, class ProA, class ProB, class Epi>
+template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, class ProA, class ProB,
+          class Epi>
 __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                     int M, int N, int K, const ProA& proA, const ProB& proB,
                                                     const Epi& epi, int* status, void* smem_raw) {
@@ -835,7 +836,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     constexpr uint32_t kConvBytes = 2u * kBBytes;
     constexpr uint32_t kConvOffset = RST * kRawBytes;
     constexpr uint32_t kBarOffset = kConvOffset + CST * kConvBytes;
-    constexpr uint32_t ACOLS = 2u * NMMA;         // two chunk buffers of accumulators
+    constexpr uint32_t ACOLS = (uint32_t)NACC * NMMA;  // NACC chunk buffers of accumulators
     static_assert(NMMA == 128, "pair tiles are 256 x 128");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
     static_assert(ACOLS + 64u * CST <= 512, "accumulators and A stages exceed TMEM");
@@ -847,9 +848,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     uint64_t* rempty = rfull + RST;
     uint64_t* cfull = rempty + RST;     // used on rank 0: both CTAs' converters
     uint64_t* cempty = cfull + CST;     // both CTAs: rank 0's MMA commit
-    uint64_t* tfull = cempty + CST;     // [2] both CTAs: rank 0's MMA commit
-    uint64_t* tempty = tfull + 2;       // [2] used on rank 0: both CTAs' accumulator warps
-    uint64_t* mdone = tempty + 2;       // rank 0: MMAs drained on the abort path
+    uint64_t* tfull = cempty + CST;     // [NACC] both CTAs: rank 0's MMA commit
+    uint64_t* tempty = tfull + NACC;    // [NACC] used on rank 0: both CTAs' accumulator warps
+    uint64_t* mdone = tempty + NACC;    // rank 0: MMAs drained on the abort path
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -883,7 +884,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             mt_mbar_init(&cfull[c], 2 * NCONV);
             mt_mbar_init(&cempty[c], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NACC; ++b) {
             mt_mbar_init(&tfull[b], 1);
             mt_mbar_init(&tempty[b], 16);
         }
@@ -927,8 +928,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             bool ok = true;
             const int nchunks = (nk + CHUNK - 1) / CHUNK;
             for (int ch = 0; ch < nchunks && ok; ++ch) {
-                const int tb = ch & 1;
-                if (ch >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch >> 1) - 1) & 1u, abort_flag, status, 2)) {
+                const int tb = ch % NACC;
+                if (ch >= NACC && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch / NACC) - 1) & 1u, abort_flag, status, 2)) {
                     ok = false;
                     break;
                 }
@@ -1002,8 +1003,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         bool ok = true;
         const int nchunks = (nk + CHUNK - 1) / CHUNK;
         for (int c = 0; c < nchunks; ++c) {
-            const int tb = c & 1;
-            if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c >> 1) & 1u, abort_flag, status, 5)) {
+            const int tb = c % NACC;
+            if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c / NACC) & 1u, abort_flag, status, 5)) {
                 ok = false;
                 break;
             }

@@ -133,7 +133,8 @@ def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
 # CTA-pair (cta_group::2) tiles: 256 x 128 per two-CTA cluster, 64 B rows per CTA.
 PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
 PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
-PAIR_CSTAGES = 4                                # tensor memory: 256 accumulator columns + 4 x 64 for A
+PAIR_NACC = 2     # accumulator buffers of 128 columns (3, with 2 converted stages, measured the same)
+PAIR_CSTAGES = (512 - 128 * PAIR_NACC) // 64    # tensor memory: accumulators + 64 columns of A per stage
 
 
 def pair_enabled() -> bool:
@@ -155,7 +156,7 @@ def _pick_pair(M: int, N: int, nb: int) -> tuple[int, int, int] | None:
 
 
 def _pair_smem_bytes(rst: int, cst: int) -> int:
-    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 5) * 8 + 16 + 1024
+    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 1) * 8 + 16 + 1024
 
 
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
@@ -240,7 +241,8 @@ class TcGemmFragment:
             # normwise at 4096^3 against 3.2e-7, above an fp32 CPU product's 3.7e-7);
             # BAL: warps 2-3 split B while warps 4-7 split A (~1% faster)
             lines.append(
-                f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, 1, true>"
+                f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, 1, true, "
+                f"{PAIR_NACC}>"
                 f"(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);")
             return "\n".join(lines)
         lines.append(
