@@ -190,6 +190,22 @@ def overflow_multi_producer(ops):
     ops.elementwise("add", out="z", operands=("c1", "c2"))
 
 
+def transposed_reduction(ops):
+    """Reduction over the first axis, spelled as in the reference's sandbox
+    (sandbox.py:177-186): the last axis of a transposed view."""
+    ops.input("X", (96, 48))
+    ops.transpose("X", out="Xt")
+    ops.reduction("sum", out="S", x="Xt", axis=-1)
+
+
+def transposed_reduction_chain(ops):
+    ops.input("X", (96, 48))
+    ops.transpose("X", out="Xt")
+    ops.elementwise("exp", out="E", operands=("Xt",))
+    ops.reduction("max", out="S", x="E", axis=-1)
+    ops.elementwise("mul", out="T", operands=("S", 0.5))
+
+
 PROGRAMS = {
     "c1": c1, "c2": c2, "c3": c3, "c3sum": c3sum, "c4_head": c4_head, "c5": c5,
     "relu_matmul_bias": relu_matmul_bias, "relu_matmul": relu_matmul, "prologue_on_a": prologue_on_a,
@@ -197,4 +213,5 @@ PROGRAMS = {
     "multi_consumer_matmul": multi_consumer_matmul, "upstream_recompute": upstream_recompute,
     "multi_producer": multi_producer, "diamond": diamond, "where_standalone": where_standalone,
     "overflow_multi_producer": overflow_multi_producer,
+    "transposed_reduction": transposed_reduction, "transposed_reduction_chain": transposed_reduction_chain,
 }
