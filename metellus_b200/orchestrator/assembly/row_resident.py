@@ -47,6 +47,15 @@ def _rows_of(t: Tensor) -> tuple[int, int]:
     return 1, s[0]
 
 
+def _same_layout(view: Tensor, owner: Tensor) -> bool:
+    """Whether a view addresses its owner's elements at the owner's own (row, col):
+    same shape and strides. A transposed view of a square matrix has the owner's shape
+    but swapped strides, so it is not row local."""
+    return (view.shape == owner.shape and view.row_stride == owner.row_stride
+            and view.col_stride == owner.col_stride
+            and (len(view.shape) != 3 or view.batch_stride == owner.batch_stride))
+
+
 def row_program_check(ops: tuple[Op, ...]) -> str | None:
     """Why ``ops`` cannot run row-resident, or None when they can."""
     produced = {op.out.name: op for op in ops}
@@ -56,7 +65,7 @@ def row_program_check(ops: tuple[Op, ...]) -> str | None:
             src = op.input
             k = kinds.get(src.name) or (kinds.get(src.buffer_key) if src.buffer_key in produced else None)
             if src.name in produced or src.buffer_key in produced:
-                if k != "vector" or (src.name not in produced and src.shape != produced[src.buffer_key].out.shape):
+                if k != "vector" or (src.name not in produced and not _same_layout(src, produced[src.buffer_key].out)):
                     return f"reduction {op.out.name!r} reads a non row-local view"
             kinds[op.out.name] = "scalar"
         elif isinstance(op, ElementwiseOp):
@@ -68,7 +77,7 @@ def row_program_check(ops: tuple[Op, ...]) -> str | None:
                 if owner is None:
                     continue
                 ko = kinds[owner]
-                if ko == "vector" and (o.name != owner and o.shape != produced[owner].out.shape):
+                if ko == "vector" and (o.name != owner and not _same_layout(o, produced[owner].out)):
                     return f"{op.out.name!r} reads a reshaped view of row vector {owner!r}"
                 if ko == "scalar" and _is_vector_tensor(o):
                     return f"{op.out.name!r} reads per-row scalar {owner!r} as a full row"

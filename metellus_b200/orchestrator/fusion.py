@@ -151,9 +151,12 @@ def try_elem_chain_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) -> G
         p = head.operands[0]
         if not isinstance(p, Tensor) or p.name != tail:
             continue
-        if (u.op_ids | v.op_ids) in blacklist:
+        if (u.op_ids | v.op_ids) in blacklist or not _views_local(u.ops + v.ops):
             continue
-        return graph.replace(absorbed=(u, v), ops=u.ops + v.ops)
+        try:
+            return graph.replace(absorbed=(u, v), ops=u.ops + v.ops)
+        except ValueError:  # not convex once view reads count as edges
+            continue
     return None
 
 
@@ -182,9 +185,12 @@ def try_epilogue_absorb(graph: Graph, blacklist: frozenset[frozenset[int]]) -> G
             p = head.operands[0]
             if not (isinstance(p, Tensor) and p.name == tail):
                 continue
-        if (a.op_ids | v.op_ids) in blacklist:
+        if (a.op_ids | v.op_ids) in blacklist or not _views_local(a.ops + v.ops):
             continue
-        return graph.replace(absorbed=(a, v), ops=a.ops + v.ops)
+        try:
+            return graph.replace(absorbed=(a, v), ops=a.ops + v.ops)
+        except ValueError:  # not convex once view reads count as edges
+            continue
     return None
 
 
@@ -211,6 +217,35 @@ def _anchor_boundary_input_names(anchor: Op, vertex: Vertex) -> set[str]:
             cur = p.name
         out.add(cur)
     return out
+
+
+def _view_is_local(view: Tensor, owner: Tensor) -> bool:
+    """Whether a kernel that computes ``owner`` element by element can hand that value
+    to a read of ``view`` at the same index: an identity view (same shape and strides),
+    or a per-row vector in another shape ((M,) <-> (M, 1)). A transposed or reshaped
+    view of a tensor produced in the same kernel reads elements another thread or
+    block computes."""
+    if (view.shape == owner.shape and view.row_stride == owner.row_stride
+            and view.col_stride == owner.col_stride
+            and (len(view.shape) != 3 or view.batch_stride == owner.batch_stride)):
+        return True
+    rv, ro = _row_space(view), _row_space(owner)
+    return rv == ro and rv[1] is None
+
+
+def _views_local(ops: tuple[Op, ...]) -> bool:
+    """No op of a prospective kernel reads a non-local view (``_view_is_local``) of a
+    tensor another op of the same kernel produces. The reference's fusion rules do not
+    check this (its chain rule fuses ``y = t + transpose(t)`` with ``t``'s producer and
+    reads ``t`` from memory that the same kernel is still writing); every merge here
+    does."""
+    produced = {op.out.name: op.out for op in ops}
+    for op in ops:
+        for t in op.inputs:
+            owner = produced.get(t.buffer_key)
+            if owner is not None and t.name != owner.name and not _view_is_local(t, owner):
+                return False
+    return True
 
 
 def _merge_in_order(graph: Graph, *vertices: Vertex) -> tuple[Op, ...]:
@@ -240,9 +275,12 @@ def try_prologue_absorb_single(graph: Graph, blacklist: frozenset[frozenset[int]
             continue
         if not all(_prologue_eligible(op) for op in v.ops if isinstance(op, ElementwiseOp)):
             continue
-        if (v.op_ids | a.op_ids) in blacklist:
+        if (v.op_ids | a.op_ids) in blacklist or not _views_local(_merge_in_order(graph, v, a)):
             continue
-        return graph.replace(absorbed=(v, a), ops=_merge_in_order(graph, v, a))
+        try:
+            return graph.replace(absorbed=(v, a), ops=_merge_in_order(graph, v, a))
+        except ValueError:  # not convex once view reads count as edges
+            continue
     return None
 
 
@@ -269,9 +307,12 @@ def try_multi_producer_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) 
             continue
         if ax.out.shape != ay.out.shape:
             continue
-        if (px.op_ids | py.op_ids | v.op_ids) in blacklist:
+        if (px.op_ids | py.op_ids | v.op_ids) in blacklist or not _views_local(_merge_in_order(graph, px, py, v)):
             continue
-        return graph.replace(absorbed=(px, py, v), ops=_merge_in_order(graph, px, py, v))
+        try:
+            return graph.replace(absorbed=(px, py, v), ops=_merge_in_order(graph, px, py, v))
+        except ValueError:  # not convex once view reads count as edges
+            continue
     return None
 
 
@@ -310,7 +351,7 @@ def try_prologue_absorb_multi(graph: Graph, blacklist: frozenset[frozenset[int]]
         for aid in ids:
             cur = next(cv for cv in g.vertices if any(id(op) == aid for op in cv.ops))
             g = g.absorb_into(cur, v.ops)
-        still = out in graph.program_outputs or any(out in o.inputs for o in g.vertices if o is not v)
+        still = out in graph.program_outputs or any(out in g.reads(o) for o in g.vertices if o is not v)
         if not still:
             g = g.remove_vertex(v)
         return g
@@ -358,7 +399,10 @@ def _edges(graph: Graph) -> list[tuple[Vertex, Vertex]]:
 
 def _try_merge(graph: Graph, u: Vertex, v: Vertex) -> Graph | None:
     try:
-        g = graph.replace(absorbed=(u, v), ops=_merge_in_order(graph, u, v))
+        ops = _merge_in_order(graph, u, v)
+        if not _views_local(ops):
+            return None
+        g = graph.replace(absorbed=(u, v), ops=ops)
     except ValueError:
         return None
     return g if _views_ordered(g) else None
@@ -438,6 +482,14 @@ def try_row_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) -> Graph | 
             continue
         if (u.op_ids | v.op_ids) in blacklist:
             continue
+        from metellus_b200.orchestrator.assembly.row_resident import row_program_check
+
+        try:
+            merged = _merge_in_order(graph, u, v)
+        except ValueError:
+            continue
+        if row_program_check(merged) is not None:
+            continue  # e.g. a reduction over a transposed view of a row it would hold
         g = _try_merge(graph, u, v)
         if g is not None:
             return g
@@ -519,7 +571,10 @@ def try_dual_gemm_fuse(graph: Graph, blacklist: frozenset[frozenset[int]]) -> Gr
             if frozenset(o for v in region for o in v.op_ids) in blacklist:
                 continue
             try:
-                g = graph.replace(absorbed=tuple(region), ops=_merge_in_order(graph, *region))
+                ops = _merge_in_order(graph, *region)
+                if not _views_local(ops):
+                    continue
+                g = graph.replace(absorbed=tuple(region), ops=ops)
             except ValueError:
                 continue
             if _views_ordered(g):

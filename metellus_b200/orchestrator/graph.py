@@ -10,7 +10,7 @@ verifies every producer->consumer edge of the original program is still respecte
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 from metellus_b200.orchestrator.ir import Op, Program
 
@@ -35,6 +35,9 @@ class Graph:
     vertices: tuple[Vertex, ...]
     op_index: dict[int, int]
     program_outputs: frozenset[str]
+    # view name -> storage owner, for every view an op reads (transpose / reshape): a
+    # vertex reading a view depends on, and keeps materialised, the owner's producer
+    view_owner: dict[str, str] = field(default_factory=dict, compare=False)
 
     @classmethod
     def from_program(
@@ -42,7 +45,8 @@ class Graph:
     ) -> Graph:
         op_index = {id(op): i for i, op in enumerate(program)}
         produced = {op.out.name for op in program}
-        used = {t.name for op in program for t in op.inputs}
+        view_owner = {t.name: t.buffer_key for op in program for t in op.inputs if t.name != t.buffer_key}
+        used = {t.name for op in program for t in op.inputs} | set(view_owner.values())
         outs = frozenset(produced - used) if program_outputs is None else frozenset(program_outputs)
         vertices = []
         for op in program:
@@ -50,12 +54,18 @@ class Graph:
             visible = name in used or name in outs
             vertices.append(Vertex(ops=(op,), inputs=tuple(t.name for t in op.inputs),
                                    outputs=(name,) if visible else ()))
-        return cls(vertices=tuple(vertices), op_index=op_index, program_outputs=outs)
+        return cls(vertices=tuple(vertices), op_index=op_index, program_outputs=outs, view_owner=view_owner)
 
     # -- rewrites ------------------------------------------------------------------
 
     def _with(self, vertices: tuple[Vertex, ...]) -> Graph:
-        return Graph(vertices=vertices, op_index=self.op_index, program_outputs=self.program_outputs)
+        return Graph(vertices=vertices, op_index=self.op_index, program_outputs=self.program_outputs,
+                     view_owner=self.view_owner)
+
+    def reads(self, v: Vertex) -> set[str]:
+        """Names ``v`` reads: its inputs plus the storage owner of every view among
+        them."""
+        return set(v.inputs) | {self.view_owner[n] for n in v.inputs if n in self.view_owner}
 
     def replace(self, absorbed: tuple[Vertex, ...], ops: tuple[Op, ...]) -> Graph:
         """Collapse ``absorbed`` into one vertex holding ``ops`` (graph.py:118-212)."""
@@ -79,7 +89,7 @@ class Graph:
         still_read: set[str] = set()
         for v in self.vertices:
             if id(v) not in taken:
-                still_read.update(v.inputs)
+                still_read.update(self.reads(v))
         read_by_absorbed: set[str] = set()
         for v in absorbed:
             read_by_absorbed.update(v.inputs)
@@ -140,7 +150,7 @@ class Graph:
             if name in self.program_outputs:
                 raise ValueError(f"remove_vertex: output {name!r} is a program output; cannot remove")
             for other in self.vertices:
-                if other is not vertex and name in other.inputs:
+                if other is not vertex and name in self.reads(other):
                     raise ValueError(f"remove_vertex: output {name!r} still consumed by another vertex")
         return self._with(tuple(v for v in self.vertices if v is not vertex))
 
@@ -156,7 +166,7 @@ class Graph:
         succ: list[set[int]] = [set() for _ in range(n)]
         indeg = [0] * n
         for i, v in enumerate(self.vertices):
-            deps = {producer[nm] for nm in v.inputs if nm in producer}
+            deps = {producer[nm] for nm in self.reads(v) if nm in producer and producer[nm] != i}
             indeg[i] = len(deps)
             for d in deps:
                 succ[d].add(i)
@@ -224,4 +234,5 @@ class Graph:
         return None
 
     def consumers_of(self, name: str) -> tuple[Vertex, ...]:
-        return tuple(v for v in self.topo_sort() if name in v.inputs)
+        """Vertices that read ``name`` directly or through a view of it."""
+        return tuple(v for v in self.topo_sort() if name in self.reads(v))

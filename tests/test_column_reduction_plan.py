@@ -63,3 +63,36 @@ def test_oracle_reads_transposed_views():
     ops.transpose("X", out="Xt")
     ops.reduction("sum", out="R", x="Xt")
     np.testing.assert_array_equal(evaluate(ops, np.float64)["R"], X.astype(np.float64).sum(axis=0))
+
+
+def _square_transpose_programs():
+    """Programs reading a transposed view of a tensor computed in the same program, on
+    a square shape (the view has the owner's shape but swapped strides)."""
+    out = {}
+    ops = Operations()
+    ops.from_numpy(np.arange(64 * 64, dtype=np.float32).reshape(64, 64) / 4096, "x")
+    ops.elementwise("exp", "t", ("x",))
+    ops.transpose("t", out="tt")
+    ops.reduction("sum", out="s", x="tt")
+    out["colsum"] = ops
+    ops = Operations()
+    ops.from_numpy(np.arange(64 * 64, dtype=np.float32).reshape(64, 64) / 4096, "x")
+    ops.elementwise("exp", "t", ("x",))
+    ops.transpose("t", out="tt")
+    ops.elementwise("add", "y", ("t", "tt"))
+    out["symmetrise"] = ops
+    return out
+
+
+@pytest.mark.parametrize("name", ["colsum", "symmetrise"])
+def test_transposed_view_of_an_inner_product_is_not_fused(name):
+    """A kernel that computes t element by element cannot also read transpose(t): the
+    producer of t and the reader of its transposed view must be separate kernels (the
+    reference's chain rule fuses ``t + transpose(t)`` and reads t before it is written)."""
+    ops = _square_transpose_programs()[name]
+    for g in compile_program(ops):
+        names = {op.out.name for op in g.ops}
+        for op in g.ops:
+            for t in op.inputs:
+                if t.name == "tt":
+                    assert "t" not in names, (g.strategy, names)

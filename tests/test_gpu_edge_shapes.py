@@ -106,3 +106,21 @@ def test_row_fused_value_with_second_consumer(cuda_device):
     res = run(ops)
     r64, r32 = evaluate(ops, np.float64), evaluate(ops, np.float32)
     assert_matmul_close(res.env["t3"], r64["t3"], r32["t3"], what="row-fused second consumer")
+
+
+@pytest.mark.parametrize("kind", ["colsum", "symmetrise"])
+def test_transposed_view_of_inner_product(cuda_device, kind):
+    """t = exp(x) on a square x, then sum(transpose(t)) or t + transpose(t): the reads
+    of the transposed view must see all of t (separate kernels), matching the oracle."""
+    r = np.random.default_rng(21)
+    ops = Operations()
+    ops.from_numpy(r.normal(0, 1, (192, 192)).astype(np.float32), "x")
+    ops.elementwise("exp", "t", ("x",))
+    ops.transpose("t", out="tt")
+    if kind == "colsum":
+        ops.reduction("sum", out="y", x="tt")
+    else:
+        ops.elementwise("add", "y", ("t", "tt"))
+    res = run(ops)
+    ref = evaluate(ops, np.float64)["y"]
+    np.testing.assert_allclose(res.env["y"], ref, rtol=2e-6, atol=0)

@@ -1,6 +1,7 @@
 """Property tests of the planner on random programs (CPU only: plans and generated
 source, no launches). For seeded random mixes of elementwise chains and DAGs,
-row / column broadcasts, last-axis reductions with views, matmuls and diamonds:
+row / column broadcasts, last-axis reductions with views (including first-axis
+reductions through a transposed view), matmuls and diamonds:
 
 * every op lands in exactly one kernel group, and the groups' ops in dispatch order
   respect every producer -> consumer edge of the program;
@@ -54,8 +55,8 @@ def random_program(seed: int, safe: bool = False, large: bool = False) -> Operat
         return name
     for k in range(int(r.integers(3, 11))):
         kind = r.choice(["unary", "binary", "scalar", "rowb", "softmaxish", "matmul", "diamond", "gated", "onp",
-                         "tmatmul"],
-                        p=[0.16, 0.16, 0.11, 0.08, 0.12, 0.08, 0.08, 0.1, 0.06, 0.05])
+                         "tmatmul", "colred"],
+                        p=[0.13, 0.14, 0.11, 0.08, 0.11, 0.08, 0.08, 0.1, 0.06, 0.05, 0.06])
         out = f"t{k}"
         if kind == "unary":
             ops.elementwise(str(r.choice(unary)), out=out, operands=(str(r.choice(mats)),))
@@ -99,6 +100,14 @@ def random_program(seed: int, safe: bool = False, large: bool = False) -> Operat
                 ops.transpose(need("WT"), out="WTt")
             ops.matmul(a=str(r.choice(mats)), b="WTt", out=out)
             others[out] = (M, P)
+        elif kind == "colred":  # reduce over the first axis (a transposed view), add back as a row
+            src = str(r.choice(mats))
+            ops.transpose(src, out=f"{out}_T")
+            ops.reduction(str(r.choice(["max", "min"] if safe else ["max", "sum"])), out=f"{out}_r", x=f"{out}_T",
+                          axis=-1)
+            ops.reshape(f"{out}_r", (1, N), out=f"{out}_row")
+            ops.elementwise("add", out=out, operands=(str(r.choice(mats)), f"{out}_row"), y_broadcast="row")
+            mats.append(out)
         elif others:  # an elementwise op over (M, P) results
             a = str(r.choice(list(others)))
             ops.elementwise(str(r.choice(unary)), out=out, operands=(a,))
