@@ -46,8 +46,11 @@ class Graph:
         op_index = {id(op): i for i, op in enumerate(program)}
         produced = {op.out.name for op in program}
         view_owner = {t.name: t.buffer_key for op in program for t in op.inputs if t.name != t.buffer_key}
-        used = {t.name for op in program for t in op.inputs} | set(view_owner.values())
+        used = {t.name for op in program for t in op.inputs}
+        # program outputs as the reference defines them: produced and never read by name
+        # (a tensor read only through a view is still an output)
         outs = frozenset(produced - used) if program_outputs is None else frozenset(program_outputs)
+        used |= set(view_owner.values())
         vertices = []
         for op in program:
             name = op.out.name
