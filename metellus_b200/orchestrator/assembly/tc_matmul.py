@@ -1,22 +1,27 @@
 """tcgen05 / TMEM 3xTF32 tensor-core pipe for matmul groups (B200).
 
 Every matmul strategy (standalone, register or shared-tile epilogue, elementwise
-prologue) and the two-anchor strategies (multi-producer convergent, diamond) lower to
-one warp-specialised kernel built on ``mt_gemm_3xtf32`` (csrc/include/mt_tc.cuh):
+prologue) and the two-anchor strategies (multi-producer convergent, diamond, dual GEMM)
+lower to one warp-specialised kernel from csrc/include/mt_tc.cuh:
 
-* TMA (128-byte swizzle) streams 128 x 32 A tiles and BN x 32 B tiles into a ring of
-  shared-memory stages;
-* four converter warps split each landed fp32 tile into tf32 hi / lo in place,
-  applying the prologue chain (read at the element's global (row, k)) first;
-* one thread issues ``tcgen05.mma.kind::tf32`` for hi*lo + lo*hi + hi*hi into fp32
-  TMEM accumulators (one per anchor);
-* the same four warps read the accumulators back with ``tcgen05.ld`` and run the
-  epilogue (the fused elementwise chain, or the two-anchor merge) at each element's
-  global (row, col) and store the result.
+* TMA (128-byte swizzle) streams 128 x 32 A tiles and the B tiles of every anchor into
+  a raw ring of shared-memory stages;
+* six converter warps apply the prologue chain (read at the element's global
+  (row, k)) and split each fp32 value into tf32 hi / lo: A rows into tensor memory,
+  B tiles into a converted ring in shared memory;
+* one thread issues ``tcgen05.mma.kind::tf32`` for hi*lo + lo*hi + hi*hi into a fresh
+  TMEM accumulator per 32-deep k-tile;
+* eight accumulator warps add each finished k-tile into fp32 registers and run the
+  epilogue (the fused elementwise chain, or the two-anchor merge / DAG) at each
+  element's global (row, col).
 
-The pipe is chosen per group: shapes the tensor maps cannot describe (batched
-operands, unaligned strides, an MN-major operand whose extent is not a multiple of
-32) or tiny problems stay on the SIMT FFMA pipe. ``METELLUS_TC=0`` forces FFMA.
+Tile shapes: ``mt_gemm_3xtf32_pair`` (256 x 128 per two-CTA cluster, ``cta_group::2``)
+when the output has enough such tiles to fill the SMs; otherwise ``mt_gemm_3xtf32``
+with 128 x BN tiles on one CTA, and split-K over a two-CTA cluster when even those are
+too few. Shapes the tensor maps cannot describe (batched operands, unaligned strides,
+an MN-major operand whose extent is not a multiple of 32) or tiny problems stay on the
+SIMT FFMA pipe. ``METELLUS_TC=0`` forces FFMA; ``METELLUS_TC_PAIR=0`` disables the pair
+tiles.
 """
 
 from __future__ import annotations
