@@ -301,8 +301,9 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
                     const float x = sv[16 * hh + k];
                     mt_split_tf32(x, sv[16 * hh + k], lo[k]);
                 }
-                mt_tmem_st16(pbuf + 16u * (uint32_t)hh, &sv[16 * hh]);
-                mt_tmem_st16(pbuf + 32u + 16u * (uint32_t)hh, lo);
+                mt_tmem_st16_nowait(pbuf + 16u * (uint32_t)hh, &sv[16 * hh]);
+                mt_tmem_st16_nowait(pbuf + 32u + 16u * (uint32_t)hh, lo);
+                mt_tmem_wait_st();  // before `lo` is refilled
             }
             mt_tc_fence_before();
             __syncwarp();
