@@ -53,6 +53,16 @@ __device__ __forceinline__ bool mt_mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// Non-blocking check of an mbarrier phase.
+__device__ __forceinline__ bool mt_mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(mt_smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: true when the phase completed, false on timeout or CTA abort.
 __device__ __forceinline__ bool mt_mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                              int* status, int code) {
@@ -836,6 +846,28 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     }
 }
 
+// Optional wait-time counters for the pair GEMM (compile with MT_GEMM_PROFILE): clock64
+// cycles each role spends in its mbarrier waits, summed over CTAs into the 64-bit slots
+// 1..7 of the status buffer (slot 0 stays the timeout code). Off by default.
+#ifdef MT_GEMM_PROFILE
+#define MT_PROF_DECL() unsigned long long p_mma_issue = 0, p_mma_tempty = 0, p_mma_cfull = 0, p_mma_loop = 0, \
+    p_conv_rfull = 0, p_conv_cempty = 0, p_acc_tfull = 0
+#define MT_PROF_BEGIN(t) const long long t = clock64()
+#define MT_PROF_END(t, acc) (acc) += (unsigned long long)(clock64() - (t))
+#define MT_PROF_FLUSH(st) do { \
+    unsigned long long* q = reinterpret_cast<unsigned long long*>(st); \
+    if (p_mma_cfull | p_mma_tempty | p_mma_loop) { atomicAdd(q + 1, p_mma_cfull); atomicAdd(q + 2, p_mma_tempty); \
+        atomicAdd(q + 3, p_mma_loop); } \
+    if (p_conv_rfull | p_conv_cempty) { atomicAdd(q + 4, p_conv_rfull); atomicAdd(q + 5, p_conv_cempty); } \
+    if (p_mma_issue) atomicAdd(q + 6, p_mma_issue); \
+    if (p_acc_tfull) atomicAdd(q + 7, p_acc_tfull); } while (0)
+#else
+#define MT_PROF_DECL() do { } while (0)
+#define MT_PROF_BEGIN(t) do { } while (0)
+#define MT_PROF_END(t, acc) do { } while (0)
+#define MT_PROF_FLUSH(st) do { } while (0)
+#endif
+
 // ---------------------------------------------------------------------------------
 // CTA-pair GEMM: a 256 x 128 output tile per cluster of two CTAs (cta_group::2).
 //
@@ -856,8 +888,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
 // (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
 // before tensor memory is freed and either exits.
-template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, class ProA, class ProB,
-          class Epi>
+template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, int NISSUE, class ProA,
+          class ProB, class Epi>
 __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                     int M, int N, int K, const ProA& proA, const ProB& proB,
                                                     const Epi& epi, int* status, void* smem_raw) {
@@ -874,6 +906,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     static_assert(NMMA == 128, "pair tiles are 256 x 128");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
     static_assert(ACOLS + 64u * CST <= 512, "accumulators and A stages exceed TMEM");
+    static_assert(NISSUE == 1 || (NISSUE == 2 && NACC == 2), "two issuers own one accumulator buffer each");
     constexpr uint32_t NCOLS = 512;
     constexpr int NCONV = 6;
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -884,12 +917,13 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     uint64_t* cempty = cfull + CST;     // both CTAs: rank 0's MMA commit
     uint64_t* tfull = cempty + CST;     // [NACC] both CTAs: rank 0's MMA commit
     uint64_t* tempty = tfull + NACC;    // [NACC] used on rank 0: both CTAs' accumulator warps
-    uint64_t* mdone = tempty + NACC;    // rank 0: MMAs drained on the abort path
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+    uint64_t* mdone = tempty + NACC;    // [2] rank 0: each issuer's MMAs drained on the abort path
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
     const int rank = (int)mt_cluster_rank();
+    MT_PROF_DECL();
     int m0, n0;
     {
         constexpr int kGroupM = 8;              // in 256-row pair tiles
@@ -922,7 +956,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             mt_mbar_init(&tfull[b], 1);
             mt_mbar_init(&tempty[b], 16);
         }
-        mt_mbar_init(mdone, 1);
+        mt_mbar_init(&mdone[0], 1);
+        mt_mbar_init(&mdone[1], 1);
         *abort_flag = 0;
         mt_fence_barrier_init();
     }
@@ -937,46 +972,50 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     mt_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        if (lane == 0) {
-            int issued = 0;
-            for (int kt = 0; kt < nk; ++kt) {
-                const int r = kt % RST;
-                if (kt >= RST && !mt_mbar_wait(&rempty[r], (uint32_t)((kt / RST) - 1) & 1u, abort_flag, status, 1))
-                    break;
-                mt_mbar_expect_tx(&rfull[r], kRawBytes);
-                const int kg = kt * 32;
-                mt_tma_load_2d(A_raw(r), tmA, &rfull[r], kg, m0);
-                if (B_MN) mt_tma_load_3d(B_raw(r), tmB, &rfull[r], 0, kg, nb0 / 32);
-                else mt_tma_load_2d(B_raw(r), tmB, &rfull[r], kg, nb0);
-                issued = kt + 1;
-            }
-            if (*abort_flag) {
-                for (int kt = (issued > RST ? issued - RST : 0); kt < issued; ++kt)
-                    mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
-            }
-        }
-    } else if (warp == 1) {
+    // TMA loads of k-tile kt into raw stage kt % RST; issued by lane 0 of converter
+    // warp 2 (below), so that warps 0 and 1 can both issue MMAs
+    auto tma_issue = [&](int kt) {
+        const int r = kt % RST;
+        mt_mbar_expect_tx(&rfull[r], kRawBytes);
+        const int kg = kt * 32;
+        mt_tma_load_2d(A_raw(r), tmA, &rfull[r], kg, m0);
+        if (B_MN) mt_tma_load_3d(B_raw(r), tmB, &rfull[r], 0, kg, nb0 / 32);
+        else mt_tma_load_2d(B_raw(r), tmB, &rfull[r], kg, nb0);
+    };
+
+    if (warp == 1 || (NISSUE == 2 && warp == 0)) {
+        // NISSUE = 2: warp 1 issues the even chunks and warp 0 the odd ones (with
+        // NACC = 2 each owns one accumulator buffer), so one issuer's barrier waits and
+        // fences overlap the other's MMAs: a single issuing thread leaves the tensor
+        // pipe idle for every cycle it spends between two MMAs (measured: an N-cycle
+        // gap per 12 MMAs costs ~N cycles of pipe time).
+        const int issuer = warp == 1 ? 0 : 1;
         if (rank == 0 && lane == 0) {
             constexpr uint32_t idesc = mt_idesc_tf32(256, NMMA, false, B_MN);
             bool ok = true;
             const int nchunks = (nk + CHUNK - 1) / CHUNK;
-            for (int ch = 0; ch < nchunks && ok; ++ch) {
+            MT_PROF_BEGIN(tloop);
+            for (int ch = issuer; ch < nchunks && ok; ch += NISSUE) {
                 const int tb = ch % NACC;
+                MT_PROF_BEGIN(w1);
                 if (ch >= NACC && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch / NACC) - 1) & 1u, abort_flag, status, 2)) {
                     ok = false;
                     break;
                 }
-                mt_tc_fence_after();
+                MT_PROF_END(w1, p_mma_tempty);
+                // one tcgen05.fence::after_thread_sync per k-tile, after both waits
                 const int kt0 = ch * CHUNK, kt1 = min(kt0 + CHUNK, nk);
                 const uint32_t d = tmem + (uint32_t)(tb * NMMA);
                 for (int kt = kt0; kt < kt1; ++kt) {
                     const int c = kt % CST;
+                    MT_PROF_BEGIN(w2);
                     if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
                         ok = false;
                         break;
                     }
+                    MT_PROF_END(w2, p_mma_cfull);
                     mt_tc_fence_after();
+                    MT_PROF_BEGIN(w6);
                     const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
                     const uint32_t bh = mt_smem_u32(B_cv(c, 0)), bl = mt_smem_u32(B_cv(c, 1));
 #pragma unroll
@@ -990,22 +1029,28 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                         mt_mma_tf32_ts_pair(d, dah, dbh, idesc, 1u);
                     }
                     mt_mma_commit_pair_both(&cempty[c]);
+                    MT_PROF_END(w6, p_mma_issue);
                 }
                 if (ok) mt_mma_commit_pair_both(&tfull[tb]);
             }
+            MT_PROF_END(tloop, p_mma_loop);
             if (!ok) {  // let the MMAs in flight finish before tensor memory is freed
-                mt_mma_commit_pair_local(mdone);
-                mt_mbar_drain(mdone, 0);
+                mt_mma_commit_pair_local(&mdone[issuer]);
+                mt_mbar_drain(&mdone[issuer], 0);
             }
         }
-    } else if (warp < 8) {
+    } else if (warp >= 2 && warp < 8) {
         const int cw = warp - 2;
         const int ct = cw * 32 + lane;
         const uint32_t cfull_r0 = mt_cluster_map(cfull, 0);
         for (int kt = 0; kt < nk; ++kt) {
             const int r = kt % RST, c = kt % CST;
+            MT_PROF_BEGIN(w3);
             if (!mt_mbar_wait(&rfull[r], (uint32_t)(kt / RST) & 1u, abort_flag, status, 3)) break;
+            if (warp == 4 && lane == 0) MT_PROF_END(w3, p_conv_rfull);
+            MT_PROF_BEGIN(w4);
             if (kt >= CST && !mt_mbar_wait(&cempty[c], (uint32_t)((kt / CST) - 1) & 1u, abort_flag, status, 3)) break;
+            if (warp == 4 && lane == 0) MT_PROF_END(w4, p_conv_cempty);
             mt_tc_fence_after();
             if (warp >= 4)
                 mt_convert_a_rows(A_raw(r), tmem + ACOLS + 64u * (uint32_t)c, warp & 3, lane, m0, kt * 32, M, K, proA);
@@ -1025,7 +1070,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                 mt_mbar_arrive_peer(cfull_r0 + (uint32_t)(c * 8));
             }
         }
-    } else {
+    } else if (warp >= 8) {
         const int q = warp & 3;
         const int h = (warp - 8) >> 2;
         const uint32_t tempty_r0 = mt_cluster_map(tempty, 0);
@@ -1036,26 +1081,81 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             for (int j = 0; j < HALF; ++j) acc[b][j] = 0.0f;
         bool ok = true;
         const int nchunks = (nk + CHUNK - 1) / CHUNK;
+        // lane 0 of warp 8 issues the TMA loads, refilling each raw stage as soon as the
+        // converters release it, while it waits for its accumulators (warps 0 and 1 both
+        // issue MMAs)
+        const bool tma_lane = warp == 8 && lane == 0;
+        int next_tma = 0;  // (tma_lane) first k-tile whose loads are not issued yet
+        if (tma_lane)
+            for (; next_tma < min(RST, nk); ++next_tma) tma_issue(next_tma);
+        auto pump = [&]() {
+            while (next_tma < nk && mt_mbar_test(&rempty[next_tma % RST], (uint32_t)((next_tma / RST) - 1) & 1u))
+                tma_issue(next_tma++);
+        };
         for (int c = 0; c < nchunks; ++c) {
             const int tb = c % NACC;
-            if (!mt_mbar_wait(&tfull[tb], (uint32_t)(c / NACC) & 1u, abort_flag, status, 5)) {
+            const uint32_t par = (uint32_t)(c / NACC) & 1u;
+            MT_PROF_BEGIN(w5);
+            bool landed;
+            if (tma_lane) {
+                // poll: keep the raw ring full until this chunk's accumulator is ready
+                const uint64_t t0 = mt_globaltimer();
+                for (uint32_t it = 1;; ++it) {
+                    pump();
+                    if (mt_mbar_test(&tfull[tb], par)) {
+                        landed = true;
+                        break;
+                    }
+                    if ((it & 63u) == 0) {
+                        if (*abort_flag) {
+                            landed = false;
+                            break;
+                        }
+                        if (mt_globaltimer() - t0 > MT_WAIT_LIMIT_NS) {
+                            atomicCAS(status, 0, 5);
+                            *abort_flag = 1;
+                            landed = false;
+                            break;
+                        }
+                    }
+                }
+            } else {
+                landed = mt_mbar_wait(&tfull[tb], par, abort_flag, status, 5);
+            }
+            if (!landed) {
                 ok = false;
                 break;
             }
+            if (warp == 8 && lane == 0) MT_PROF_END(w5, p_acc_tfull);
+            __syncwarp();
             mt_tc_fence_after();
+            // NB * HALF / 32 = 2 loads of 32 columns; the buffer is released as soon as
+            // the last load has landed, before its adds
+            constexpr int NLD = NB * (HALF / 32);
+            static_assert(NLD == 2, "two 32-column loads per accumulator warp");
+            float v[32];
 #pragma unroll
-            for (int b = 0; b < NB; ++b) {
+            for (int l = 0; l < NLD; ++l) {
+                const int b = l / (HALF / 32), j = l % (HALF / 32);
+                if (l > 0) {
+                    const int pb = (l - 1) / (HALF / 32), pj = (l - 1) % (HALF / 32);
 #pragma unroll
-                for (int j = 0; j < HALF / 32; ++j) {
-                    float v[32];
-                    mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * 32), v);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[b][j * 32 + i] = __fadd_rn(acc[b][j * 32 + i], v[i]);
+                    for (int i = 0; i < 32; ++i) acc[pb][pj * 32 + i] = __fadd_rn(acc[pb][pj * 32 + i], v[i]);
                 }
+                mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * 32), v);
             }
             mt_tc_fence_before();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive_peer(tempty_r0 + (uint32_t)(tb * 8));
+            {
+                constexpr int lb = (NLD - 1) / (HALF / 32), lj = (NLD - 1) % (HALF / 32);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[lb][lj * 32 + i] = __fadd_rn(acc[lb][lj * 32 + i], v[i]);
+            }
+        }
+        if (tma_lane && *abort_flag) {  // let this CTA's own copies land before it can exit
+            for (int kt = (next_tma > RST ? next_tma - RST : 0); kt < next_tma; ++kt)
+                mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
         }
         if (ok) {
             const int row = m0 + q * 32 + lane;
@@ -1070,6 +1170,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             }
         }
     }
+    MT_PROF_FLUSH(status);
     mt_tc_fence_before();
     __syncthreads();
     mt_cluster_sync();  // no CTA frees tensor memory or exits while its partner may still use it

@@ -139,6 +139,8 @@ def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
 PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
 PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
 PAIR_NACC = 2     # accumulator buffers of 128 columns (3, with 2 converted stages, measured the same)
+PAIR_ISSUERS = int(os.environ.get("METELLUS_TC_ISSUERS", "2"))  # MMA-issuing warps (warps 1 and 0)
+PAIR_THREADS = 512
 PAIR_CSTAGES = (512 - 128 * PAIR_NACC) // 64    # tensor memory: accumulators + 64 columns of A per stage
 
 
@@ -161,7 +163,7 @@ def _pick_pair(M: int, N: int, nb: int) -> tuple[int, int, int] | None:
 
 
 def _pair_smem_bytes(rst: int, cst: int) -> int:
-    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 1) * 8 + 16 + 1024
+    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 2) * 8 + 16 + 1024
 
 
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
@@ -247,7 +249,7 @@ class TcGemmFragment:
             # BAL: warps 2-3 split B while warps 4-7 split A (~1% faster)
             lines.append(
                 f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, 1, true, "
-                f"{PAIR_NACC}>"
+                f"{PAIR_NACC}, {PAIR_ISSUERS}>"
                 f"(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);")
             return "\n".join(lines)
         lines.append(
@@ -358,7 +360,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
     ctx = CodegenContext(
-        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS if pair else 512, tg_y=1,
         threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
         helpers=(header("mt_tc.cuh"),),
         extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0"),
@@ -367,7 +369,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
         grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (splitk * -(-N // bn), -(-M // 128), 1),
-        threads=(512, 1, 1), ops=decision.ops,
+        threads=(PAIR_THREADS if pair else 512, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
         cluster_x=2 if pair else splitk,
     )
@@ -433,7 +435,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_diamond_{merge.out.name}_fused"
     ctx = CodegenContext(
-        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=512, tg_y=1,
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS if pair else 512, tg_y=1,
         threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
         helpers=(header("mt_tc.cuh"),),
         extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0",
@@ -443,7 +445,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
         grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (-(-N // bn), -(-M // 128), 1),
-        threads=(512, 1, 1), ops=decision.ops,
+        threads=(PAIR_THREADS if pair else 512, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
         cluster_x=2 if pair else 1,
     )
