@@ -882,7 +882,16 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // Two anchors sharing A (NB = 2, BN = 64): rank b holds anchor b's 64 columns, so D
 // columns [0, 64) are anchor 0 and [64, 128) anchor 1, as in the one-CTA layout.
 //
-// Same warp roles as mt_gemm_3xtf32 in each CTA. Hand-offs across the pair: the odd
+// Warp roles (544 threads, 17 warps) in each CTA: warps 0 and 1 issue the MMAs (one
+// elected thread each, on the even CTA only): warp 1 the even k-tiles, warp 0 the odd
+// ones, each into its own accumulator buffer. tcgen05.mma issue from one thread keeps
+// almost nothing queued (measured: an N-cycle gap between groups of 12 MMAs costs
+// ~N cycles of tensor-pipe time), so with a single issuer every barrier wait and fence
+// between k-tiles idled the pipe; with two, one issuer's waits overlap the other's
+// MMAs. Warps 2-7 split the operands (4-7: A rows into tensor memory; 2-3: B), warps
+// 8-15 drain the accumulators and run the epilogue, warp 16 issues the TMA loads. 544
+// threads leave 96 registers per thread: the drains use 16-column tensor-memory loads.
+// Hand-offs across the pair: the odd
 // CTA's converters arrive on the even CTA's cfull (remote arrive, release at CTA
 // scope, after the proxy and tcgen05 fences), its accumulator warps on the even
 // CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
@@ -972,8 +981,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     mt_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // TMA loads of k-tile kt into raw stage kt % RST; issued by lane 0 of converter
-    // warp 2 (below), so that warps 0 and 1 can both issue MMAs
+    // TMA loads of k-tile kt into raw stage kt % RST (warp 16)
     auto tma_issue = [&](int kt) {
         const int r = kt % RST;
         mt_mbar_expect_tx(&rfull[r], kRawBytes);
@@ -983,7 +991,22 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         else mt_tma_load_2d(B_raw(r), tmB, &rfull[r], kg, nb0);
     };
 
-    if (warp == 1 || (NISSUE == 2 && warp == 0)) {
+    if (warp == 16) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kt = 0; kt < nk; ++kt) {
+                const int r = kt % RST;
+                if (kt >= RST && !mt_mbar_wait(&rempty[r], (uint32_t)((kt / RST) - 1) & 1u, abort_flag, status, 1))
+                    break;
+                tma_issue(kt);
+                issued = kt + 1;
+            }
+            if (*abort_flag) {
+                for (int kt = (issued > RST ? issued - RST : 0); kt < issued; ++kt)
+                    mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
+            }
+        }
+    } else if (warp == 1 || (NISSUE == 2 && warp == 0)) {
         // NISSUE = 2: warp 1 issues the even chunks and warp 0 the odd ones (with
         // NACC = 2 each owns one accumulator buffer), so one issuer's barrier waits and
         // fences overlap the other's MMAs: a single issuing thread leaves the tensor
@@ -1070,7 +1093,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                 mt_mbar_arrive_peer(cfull_r0 + (uint32_t)(c * 8));
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 8 && warp < 16) {
         const int q = warp & 3;
         const int h = (warp - 8) >> 2;
         const uint32_t tempty_r0 = mt_cluster_map(tempty, 0);
@@ -1081,47 +1104,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             for (int j = 0; j < HALF; ++j) acc[b][j] = 0.0f;
         bool ok = true;
         const int nchunks = (nk + CHUNK - 1) / CHUNK;
-        // lane 0 of warp 8 issues the TMA loads, refilling each raw stage as soon as the
-        // converters release it, while it waits for its accumulators (warps 0 and 1 both
-        // issue MMAs)
-        const bool tma_lane = warp == 8 && lane == 0;
-        int next_tma = 0;  // (tma_lane) first k-tile whose loads are not issued yet
-        if (tma_lane)
-            for (; next_tma < min(RST, nk); ++next_tma) tma_issue(next_tma);
-        auto pump = [&]() {
-            while (next_tma < nk && mt_mbar_test(&rempty[next_tma % RST], (uint32_t)((next_tma / RST) - 1) & 1u))
-                tma_issue(next_tma++);
-        };
         for (int c = 0; c < nchunks; ++c) {
             const int tb = c % NACC;
             const uint32_t par = (uint32_t)(c / NACC) & 1u;
             MT_PROF_BEGIN(w5);
-            bool landed;
-            if (tma_lane) {
-                // poll: keep the raw ring full until this chunk's accumulator is ready
-                const uint64_t t0 = mt_globaltimer();
-                for (uint32_t it = 1;; ++it) {
-                    pump();
-                    if (mt_mbar_test(&tfull[tb], par)) {
-                        landed = true;
-                        break;
-                    }
-                    if ((it & 63u) == 0) {
-                        if (*abort_flag) {
-                            landed = false;
-                            break;
-                        }
-                        if (mt_globaltimer() - t0 > MT_WAIT_LIMIT_NS) {
-                            atomicCAS(status, 0, 5);
-                            *abort_flag = 1;
-                            landed = false;
-                            break;
-                        }
-                    }
-                }
-            } else {
-                landed = mt_mbar_wait(&tfull[tb], par, abort_flag, status, 5);
-            }
+            const bool landed = mt_mbar_wait(&tfull[tb], par, abort_flag, status, 5);
             if (!landed) {
                 ok = false;
                 break;
@@ -1129,33 +1116,32 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             if (warp == 8 && lane == 0) MT_PROF_END(w5, p_acc_tfull);
             __syncwarp();
             mt_tc_fence_after();
-            // NB * HALF / 32 = 2 loads of 32 columns; the buffer is released as soon as
-            // the last load has landed, before its adds
-            constexpr int NLD = NB * (HALF / 32);
-            static_assert(NLD == 2, "two 32-column loads per accumulator warp");
-            float v[32];
+            // NB * HALF / 16 loads of 16 columns (544 threads leave 96 registers per
+            // thread: 64 accumulators + 16 loaded values); the buffer is released as
+            // soon as the last load has landed, before its adds
+            constexpr int W = 16;
+            constexpr int PER = HALF / W;
+            constexpr int NLD = NB * PER;
+            float v[W];
 #pragma unroll
             for (int l = 0; l < NLD; ++l) {
-                const int b = l / (HALF / 32), j = l % (HALF / 32);
+                const int b = l / PER, j = l % PER;
                 if (l > 0) {
-                    const int pb = (l - 1) / (HALF / 32), pj = (l - 1) % (HALF / 32);
+                    const int pb = (l - 1) / PER, pj = (l - 1) % PER;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[pb][pj * 32 + i] = __fadd_rn(acc[pb][pj * 32 + i], v[i]);
+                    for (int i = 0; i < W; ++i) acc[pb][pj * W + i] = __fadd_rn(acc[pb][pj * W + i], v[i]);
                 }
-                mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * 32), v);
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * W);
+                mt_tmem_ld16(ta, v);
             }
             mt_tc_fence_before();
             __syncwarp();
             if (lane == 0) mt_mbar_arrive_peer(tempty_r0 + (uint32_t)(tb * 8));
             {
-                constexpr int lb = (NLD - 1) / (HALF / 32), lj = (NLD - 1) % (HALF / 32);
+                constexpr int lb = (NLD - 1) / PER, lj = (NLD - 1) % PER;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[lb][lj * 32 + i] = __fadd_rn(acc[lb][lj * 32 + i], v[i]);
+                for (int i = 0; i < W; ++i) acc[lb][lj * W + i] = __fadd_rn(acc[lb][lj * W + i], v[i]);
             }
-        }
-        if (tma_lane && *abort_flag) {  // let this CTA's own copies land before it can exit
-            for (int kt = (next_tma > RST ? next_tma - RST : 0); kt < next_tma; ++kt)
-                mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
         }
         if (ok) {
             const int row = m0 + q * 32 + lane;

@@ -139,8 +139,8 @@ def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
 PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
 PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
 PAIR_NACC = 2     # accumulator buffers of 128 columns (3, with 2 converted stages, measured the same)
-PAIR_ISSUERS = int(os.environ.get("METELLUS_TC_ISSUERS", "2"))  # MMA-issuing warps (warps 1 and 0)
-PAIR_THREADS = 512
+PAIR_ISSUERS = 2    # MMA-issuing threads (warps 1 and 0: even / odd k-tiles); 1 measured 7-10 % slower
+PAIR_THREADS = 544  # 17 warps: the 17th issues the TMA loads
 PAIR_CSTAGES = (512 - 128 * PAIR_NACC) // 64    # tensor memory: accumulators + 64 columns of A per stage
 
 
