@@ -559,9 +559,11 @@ __device__ __forceinline__ void mt_convert_a_rows(const float* tile, uint32_t t_
 
 // C-tile = A(128 x K) * B_b(K x BN) for b < NB (NB = 2: two anchors sharing A).
 //
-// 512 threads, 16 warps:
-//   warp 0       TMA producer (one elected lane)
-//   warp 1       TMEM owner + MMA issuer (one elected lane)
+// 544 threads, 17 warps:
+//   warps 0, 1   MMA issuers (one elected lane each: warp 1 the even chunks, warp 0
+//                the odd ones, each into its own accumulator buffer; see the pair
+//                kernel below for why); warp 1 also owns tensor memory
+//   warp 16      TMA producer (one elected lane)
 //   warps 2..7   converters: warps 4..7 split the A rows of their TMEM lane quarter
 //                into tf32 hi / lo in tensor memory (the MMA reads A from there, so
 //                shared memory carries only the TMA write and one read of A); then
@@ -682,7 +684,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
     mt_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp == 16) {
         if (lane == 0) {
             int issued = 0;
             for (int kt = 0; kt < nk; ++kt) {
@@ -704,11 +706,14 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                     mt_mbar_drain(&rfull[kt % RST], (uint32_t)(kt / RST) & 1u);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 0 || warp == 1) {
+        // two MMA issuers: warp 1 the even chunks, warp 0 the odd ones, each into its
+        // own accumulator buffer, so one issuer's waits overlap the other's MMAs
+        const int issuer = warp == 1 ? 0 : 1;
         if (lane == 0) {
             constexpr uint32_t idesc = mt_idesc_tf32(128, NB * BN, false, B_MN);
             bool ok = true;
-            for (int ch = 0; ch < nchunks && ok; ++ch) {
+            for (int ch = issuer; ch < nchunks && ok; ch += 2) {
                 const int tb = ch & 1;
                 if (ch >= 2 && !mt_mbar_wait(&tempty[tb], (uint32_t)((ch >> 1) - 1) & 1u, abort_flag, status, 2))
                     break;
@@ -739,7 +744,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                 mt_mma_commit(&tfull[tb]);
             }
         }
-    } else if (warp < 8) {
+    } else if (warp >= 2 && warp < 8) {
         const int cw = warp - 2;                    // converter warp 0..5
         const int ct = cw * 32 + lane;              // 0..191
         for (int kt = 0; kt < nk; ++kt) {
@@ -764,7 +769,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                 mt_mbar_arrive(&cfull[c]);
             }
         }
-    } else {
+    } else if (warp >= 8 && warp < 16) {
         const int q = warp & 3;                     // TMEM lane quarter
         const int h = (warp - 8) >> 2;              // column half
         float acc[NB][HALF];
@@ -783,11 +788,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
 #pragma unroll
-                for (int j = 0; j < HALF / 32; ++j) {
-                    float v[32];
-                    mt_tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((tb * NB + b) * BN + h * HALF + j * 32), v);
+                for (int j = 0; j < HALF / 16; ++j) {  // 16-column loads: 96 registers at 544 threads
+                    float v[16];
+                    mt_tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((tb * NB + b) * BN + h * HALF + j * 16), v);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[b][j * 32 + i] = __fadd_rn(acc[b][j * 32 + i], v[i]);
+                    for (int i = 0; i < 16; ++i) acc[b][j * 16 + i] = __fadd_rn(acc[b][j * 16 + i], v[i]);
                 }
             }
             mt_tc_fence_before();

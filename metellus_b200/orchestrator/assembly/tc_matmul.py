@@ -140,7 +140,7 @@ PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
 PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
 PAIR_NACC = 2     # accumulator buffers of 128 columns (3, with 2 converted stages, measured the same)
 PAIR_ISSUERS = 2    # MMA-issuing threads (warps 1 and 0: even / odd k-tiles); 1 measured 7-10 % slower
-PAIR_THREADS = 544  # 17 warps: the 17th issues the TMA loads
+PAIR_THREADS = 544  # 17 warps (both GEMM kernels): the 17th issues the TMA loads
 PAIR_CSTAGES = (512 - 128 * PAIR_NACC) // 64    # tensor memory: accumulators + 64 columns of A per stage
 
 
@@ -360,7 +360,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
     ctx = CodegenContext(
-        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS if pair else 512, tg_y=1,
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS, tg_y=1,
         threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
         helpers=(header("mt_tc.cuh"),),
         extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0"),
@@ -369,7 +369,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
         grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (splitk * -(-N // bn), -(-M // 128), 1),
-        threads=(PAIR_THREADS if pair else 512, 1, 1), ops=decision.ops,
+        threads=(PAIR_THREADS, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
         cluster_x=2 if pair else splitk,
     )
@@ -435,7 +435,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_diamond_{merge.out.name}_fused"
     ctx = CodegenContext(
-        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS if pair else 512, tg_y=1,
+        function_name=fn, buffers=params, dims=("M", "K", "N"), tg_x=PAIR_THREADS, tg_y=1,
         threadgroup_decls=(f"smem float tc_arena[{n_arena}];",),
         helpers=(header("mt_tc.cuh"),),
         extra_params=("const __grid_constant__ mt_tmap tm_a", "const __grid_constant__ mt_tmap tm_b0",
@@ -445,7 +445,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     return KernelGroup(
         kernel=Kernel(fragments=(frag,), ctx=ctx), bindings=bindings, dims=(M, K, N),
         grid=(2 * -(-N // bn), -(-M // 256), 1) if pair else (-(-N // bn), -(-M // 128), 1),
-        threads=(PAIR_THREADS if pair else 512, 1, 1), ops=decision.ops,
+        threads=(PAIR_THREADS, 1, 1), ops=decision.ops,
         strategy=decision.strategy, pipe="tcgen05", tmaps=tmaps, scratch=((STATUS_KEY, STATUS_BYTES),),
         cluster_x=2 if pair else 1,
     )
