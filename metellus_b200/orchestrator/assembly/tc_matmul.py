@@ -4,13 +4,14 @@ Every matmul strategy (standalone, register or shared-tile epilogue, elementwise
 prologue) and the two-anchor strategies (multi-producer convergent, diamond, dual GEMM)
 lower to one warp-specialised kernel from csrc/include/mt_tc.cuh:
 
-* TMA (128-byte swizzle) streams 128 x 32 A tiles and the B tiles of every anchor into
-  a raw ring of shared-memory stages;
+* a TMA warp (128-byte swizzle) streams 128 x 32 A tiles and the B tiles of every
+  anchor into a raw ring of shared-memory stages;
 * six converter warps apply the prologue chain (read at the element's global
   (row, k)) and split each fp32 value into tf32 hi / lo: A rows into tensor memory,
   B tiles into a converted ring in shared memory;
-* one thread issues ``tcgen05.mma.kind::tf32`` for hi*lo + lo*hi + hi*hi into a fresh
-  TMEM accumulator per 32-deep k-tile;
+* two threads (even / odd k-tiles) issue ``tcgen05.mma.kind::tf32`` for hi*lo + lo*hi +
+  hi*hi into a fresh TMEM accumulator per 32-deep k-tile (one issuer alone leaves the
+  tensor pipe idle while it waits on barriers);
 * eight accumulator warps add each finished k-tile into fp32 registers and run the
   epilogue (the fused elementwise chain, or the two-anchor merge / DAG) at each
   element's global (row, col).
