@@ -135,7 +135,7 @@ class Tensor:
     def transpose(self, name: str) -> Tensor:
         """Logical transpose of the inner matrix, no data movement (ir.py:154-174)."""
         if len(self.shape) not in (2, 3):
-            raise ValueError(f"transpose needs a 2D or batched 2D tensor; got shape {self.shape}")
+            raise ValueError(f"transpose is 2D-only (a 2D or batched 2D tensor); got shape {self.shape}")
         new_layout = Layout.COL_MAJOR if self.layout is Layout.ROW_MAJOR else Layout.ROW_MAJOR
         if len(self.shape) == 2:
             M, N = self.shape

@@ -1,0 +1,68 @@
+"""The reference's own unit tests, run against this package (CPU, no GPU).
+
+Where the reference checkout is present (this is the container the fixtures are made
+in; the GPU box has none, and the test skips there), its test files under ``tests/``
+are run in a child pytest with ``tests/reference_alias.py`` mapping its module names
+to this package. Every reference test must pass except the ones listed in
+``EXPECTED_FAILURES``, each for a stated reason: assertions on Metal Shading Language
+text (this backend emits CUDA C++), end-to-end launches (need a GPU; covered by the
+``-m gpu`` tests), the fusion budget cap (re-derived for the B200's 227 KB of shared
+memory per block instead of Apple's 32 KB), and batched-tensor extensions."""
+
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+REF_TESTS = Path("/root/reference/tests")
+ROOT = Path(__file__).resolve().parents[1]
+
+MSL = "asserts on Metal Shading Language kernel text"
+GPU = "end-to-end launch: needs a GPU (the -m gpu tests cover these paths)"
+CAP = "budget cap re-derived for 227 KB of shared memory per block (fits at 64x64)"
+BATCH = "3-D (batched) tensors are supported here"
+
+EXPECTED_FAILURES = {
+    "test_fusion.py::test_assemble_multi_producer_has_two_accumulator_sets": MSL,
+    "test_fusion.py::test_assemble_diamond_shared_emits_single_a_tile": MSL,
+    "test_fusion.py::test_assemble_relu_matmul_bias_contains_chain_markers": MSL,
+    "test_fusion.py::test_assemble_register_epilogue_uses_thread_elements": MSL,
+    "test_fusion.py::test_assemble_standalone_where_loads_cond_operand": MSL,
+    "test_fusion.py::test_assemble_1d_elementwise_uses_column_extent_one": MSL,
+    "test_fusion.py::test_assemble_binary_same_input_does_not_duplicate_base_binding": MSL,
+    "test_fusion.py::test_assemble_chain_reuses_in_chain_secondary_value": MSL,
+    "test_fusion.py::test_assemble_secondary_view_uses_col_stride": MSL,
+    "test_shape_transforms.py::test_assembled_shape_kernel_uses_input_strides": MSL,
+    "test_reshape.py::test_transposed_input_threads_through_to_matmul_kernel": MSL,
+    "test_shape_transforms.py::test_e2e_transpose_then_flatten": GPU,
+    "test_shape_transforms.py::test_e2e_transpose_then_2d_reshape": GPU,
+    "test_shape_transforms.py::test_e2e_partial_block_tail_handled": GPU,
+    "test_shape_transforms.py::test_e2e_grid_covers_multi_block_count": GPU,
+    "test_fusion_budget.py::test_overflowing_multi_producer_gets_blacklisted_and_splits": CAP,
+    "test_fusion_budget.py::test_blacklisted_fusion_still_allows_other_fusions": CAP,
+    "test_reshape.py::test_reshape_view_raises_on_3d": BATCH,
+}
+
+
+@pytest.mark.skipif(not REF_TESTS.is_dir(), reason="reference checkout not present")
+def test_reference_unit_tests_pass_against_this_package(tmp_path):
+    files = sorted(str(p) for p in REF_TESTS.glob("test_*.py"))
+    ini = tmp_path / "pytest.ini"
+    ini.write_text("[pytest]\n")
+    env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", PYTHONPATH=str(ROOT))
+    cmd = [sys.executable, "-m", "pytest", "-q", "-rfE", "-p", "no:cacheprovider", "-p", "tests.reference_alias",
+           "-c", str(ini), "--rootdir", str(tmp_path), *files]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    out = r.stdout + r.stderr
+    failed = set()
+    for m in re.finditer(r"^(?:FAILED|ERROR) (\S+?)(?: - |$)", out, re.M):
+        failed.add(m.group(1).rsplit("::", 1)[-1])
+    unexpected = sorted(failed - {k.rsplit("::", 1)[-1] for k in EXPECTED_FAILURES})
+    assert not unexpected, f"reference tests failing against this package: {unexpected}\n{out[-4000:]}"
+    passed = int(re.search(r"(\d+) passed", out).group(1))
+    assert passed >= 130, out[-2000:]
