@@ -23,7 +23,7 @@ REF_TESTS = Path("/root/reference/tests")
 ROOT = Path(__file__).resolve().parents[1]
 
 MSL = "asserts on Metal Shading Language kernel text"
-GPU = "end-to-end launch: needs a GPU (the -m gpu tests cover these paths)"
+GPU = "end-to-end launch: needs a GPU (tests/test_gpu_shape_transforms.py runs these cases)"
 CAP = "budget cap re-derived for 227 KB of shared memory per block (fits at 64x64)"
 BATCH = "3-D (batched) tensors are supported here"
 
