@@ -100,6 +100,11 @@ def random_program(seed: int, safe: bool = False, large: bool = False) -> Operat
                 ops.transpose(need("WT"), out="WTt")
             ops.matmul(a=str(r.choice(mats)), b="WTt", out=out)
             others[out] = (M, P)
+        elif kind == "colred" and M == N and r.random() < 0.5:  # square: add a transposed view
+            src = str(r.choice(mats))
+            ops.transpose(src, out=f"{out}_T")
+            ops.elementwise("add", out=out, operands=(str(r.choice(mats)), f"{out}_T"))
+            mats.append(out)
         elif kind == "colred":  # reduce over the first axis (a transposed view), add back as a row
             src = str(r.choice(mats))
             ops.transpose(src, out=f"{out}_T")
