@@ -214,13 +214,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128, 1) bench_pair(l
         const uint32_t bh = su32(sm + 32768), bl = su32(sm + 65536);
         const long long t0 = clock64();
         for (int it = 0; it < iters; ++it) {
-#pragma unroll
             if (DELAY) {
                 const long long d0 = clock64();
                 while (clock64() - d0 < DELAY) { }
             }
             if (FENCE) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t dd = tmem + (SWITCH ? 128u * (uint32_t)(it & 1) : 0u);
+#pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const uint32_t acc = (SWITCH ? kk : (it | kk)) ? 1u : 0u;
                 const uint32_t th = tmem + 256u + 8u * kk, tl = th + 32u;
