@@ -19,8 +19,9 @@
 // tiles: Q and P, the A operands, live in tensor memory.
 //
 // 512 threads, 16 warps:
-//   warp 0       TMA producer: Q once, then K_i / V_i into a 2-stage ring
-//   warp 1       TMEM owner + MMA issuer (QK_0, QK_1, then PV_i, QK_{i+2} per block)
+//   warp 0       TMA producer (Q once, then K_i / V_i into a 2-stage ring) and Q K
+//                issuer, in one non-blocking loop
+//   warp 1       TMEM owner + P V issuer
 //   warps 2..7   converters: split K_i and V_i into hi / lo in place
 //   warps 8..15  softmax + output: thread = (query row = TMEM lane, half h of the
 //                block's 64 keys and of the 64 output features); warp 8+q and 12+q
@@ -70,7 +71,9 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
     uint64_t* pfull = bars + 18;
     uint64_t* pempty = bars + 19;  // P V of the block done: P free, its product readable
     uint64_t* xbar = bars + 20;    // [4 quarters][2 parity]: half-row exchange
-    uint64_t* mdone = bars + 28;
+    uint64_t* mdone = bars + 28;   // P V issuer's MMAs drained
+    uint64_t* pvi = bars + 29;     // [2] P V of the block issued (not done): Q K of block + 2 may follow
+    uint64_t* qkdone = bars + 31;  // Q K issuer's MMAs drained
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* xch = reinterpret_cast<float*>(smem + L::kXch);
@@ -88,7 +91,7 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
         // arrival counts: 1 = TMA expect_tx / tcgen05.commit, 4 = one lane per Q
         // splitting warp, 6 = one lane per converter warp, 8 = one lane per softmax
         // warp, 64 = every thread of a softmax warp pair
-        for (int i = 0; i < 29; ++i) {
+        for (int i = 0; i < 32; ++i) {
             const uint32_t n = i == 1 ? 4u : (i >= 6 && i <= 9) ? 6u : (i >= 16 && i <= 18) ? 8u
                              : (i >= 20 && i <= 27) ? 64u : 1u;
             mt_mbar_init(&bars[i], n);
@@ -107,62 +110,95 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
     mt_tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    constexpr uint32_t idesc_s = mt_idesc_tf32(128, 64, false, false);
+    constexpr uint32_t idesc_o = mt_idesc_tf32(128, 64, false, true);
     if (warp == 0) {
+        // TMA loads and the Q K products, in one non-blocking loop: each pass issues
+        // whatever is ready (K_i once Q K of block i - 2 is done, V_i once P V of block
+        // i - 2 is done, Q K of block j once K_j is split, S buffer j - 2 is read and
+        // P V of block j - 2 is issued, which keeps P V ahead of the next Q K in the
+        // tensor pipe). Issuing Q K here and P V from warp 1 lets one thread's barrier
+        // waits overlap the other's MMAs (the tensor pipe queues almost nothing beyond
+        // the MMA in flight, so a lone issuer idles it while it waits).
         if (lane == 0) {
             mt_mbar_expect_tx(qfull, 32768);
             mt_tma_load_3d(Qs(0), tmQ, qfull, 0, q0, bz);
             mt_tma_load_3d(Qs(1), tmQ, qfull, 32, q0, bz);
-            int kiss = 0, viss = 0;
-            for (int i = 0; i < nb; ++i) {
-                const int s = i & 1;
-                const uint32_t par = (uint32_t)((i >> 1) - 1) & 1u;
-                if (i >= 2 && !mt_mbar_wait(&kempty[s], par, abort_flag, status, 1)) break;
-                mt_mbar_expect_tx(&kfull[s], 16384);
-                mt_tma_load_3d(Khi(s), tmK, &kfull[s], 0, i * 64, bz);
-                mt_tma_load_3d(Khi(s) + 2048, tmK, &kfull[s], 32, i * 64, bz);
-                kiss = i + 1;
-                if (i >= 2 && !mt_mbar_wait(&vempty[s], par, abort_flag, status, 1)) break;
-                mt_mbar_expect_tx(&vfull[s], 16384);
-                mt_tma_load_4d(Vhi(s), tmV, &vfull[s], 0, i * 64, 0, bz);
-                mt_tma_load_4d(Vhi(s) + 2048, tmV, &vfull[s], 0, i * 64 + 32, 0, bz);
-                viss = i + 1;
+            int kl = 0, vl = 0, qk = 0;
+            bool qready = false, issued_mma = false;
+            uint64_t last = mt_globaltimer();
+            for (uint32_t it = 1; kl < nb || vl < nb || qk < nb; ++it) {
+                bool prog = false;
+                if (kl < nb && (kl < 2 || mt_mbar_test(&kempty[kl & 1], (uint32_t)((kl >> 1) - 1) & 1u))) {
+                    const int s = kl & 1;
+                    mt_mbar_expect_tx(&kfull[s], 16384);
+                    mt_tma_load_3d(Khi(s), tmK, &kfull[s], 0, kl * 64, bz);
+                    mt_tma_load_3d(Khi(s) + 2048, tmK, &kfull[s], 32, kl * 64, bz);
+                    ++kl;
+                    prog = true;
+                }
+                if (vl < nb && (vl < 2 || mt_mbar_test(&vempty[vl & 1], (uint32_t)((vl >> 1) - 1) & 1u))) {
+                    const int s = vl & 1;
+                    mt_mbar_expect_tx(&vfull[s], 16384);
+                    mt_tma_load_4d(Vhi(s), tmV, &vfull[s], 0, vl * 64, 0, bz);
+                    mt_tma_load_4d(Vhi(s) + 2048, tmV, &vfull[s], 0, vl * 64 + 32, 0, bz);
+                    ++vl;
+                    prog = true;
+                }
+                if (qk < nb) {
+                    const int s = qk & 1;
+                    if (!qready) qready = mt_mbar_test(qconv, 0);
+                    const uint32_t pprev = (uint32_t)((qk >> 1) - 1) & 1u;
+                    if (qready && mt_mbar_test(&kconv[s], (uint32_t)(qk >> 1) & 1u) &&
+                        (qk < 2 || (mt_mbar_test(&sempty[s], pprev) && mt_mbar_test(&pvi[s], pprev)))) {
+                        mt_tc_fence_after();
+                        const uint32_t d = tmem + SC + 64u * (uint32_t)s;
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const uint32_t kh = mt_smem_u32(Khi(s) + j * 2048), kl2 = mt_smem_u32(Klo(s) + j * 2048);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint32_t ah = tmem + QC + 64u * (uint32_t)j + 8u * (uint32_t)kk;
+                                const uint64_t bh = mt_operand_desc_k(kh, kk), bl = mt_operand_desc_k(kl2, kk);
+                                mt_mma_tf32_ts(d, ah, bl, idesc_s, (j | kk) ? 1u : 0u);
+                                mt_mma_tf32_ts(d, ah + 32u, bh, idesc_s, 1u);
+                                mt_mma_tf32_ts(d, ah, bh, idesc_s, 1u);
+                            }
+                        }
+                        mt_mma_commit(&kempty[s]);
+                        mt_mma_commit(&sfull[s]);
+                        issued_mma = true;
+                        ++qk;
+                        prog = true;
+                    }
+                }
+                if (prog) {
+                    last = mt_globaltimer();
+                    continue;
+                }
+                __nanosleep(20);  // leave issue slots to the softmax warps sharing this scheduler
+                if ((it & 63u) == 0) {
+                    if (*abort_flag) break;
+                    if (mt_globaltimer() - last > MT_WAIT_LIMIT_NS) {
+                        atomicCAS(status, 0, 1);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+            }
+            if (issued_mma) {  // all Q K products complete before TMEM can be released (bounded)
+                mt_mma_commit(qkdone);
+                mt_mbar_drain(qkdone, 0);
             }
             if (*abort_flag) {  // let this CTA's own copies land before it can exit
                 mt_mbar_drain(qfull, 0);
-                for (int i = (kiss > 2 ? kiss - 2 : 0); i < kiss; ++i) mt_mbar_drain(&kfull[i & 1], (uint32_t)(i >> 1) & 1u);
-                for (int i = (viss > 2 ? viss - 2 : 0); i < viss; ++i) mt_mbar_drain(&vfull[i & 1], (uint32_t)(i >> 1) & 1u);
+                for (int i = (kl > 2 ? kl - 2 : 0); i < kl; ++i) mt_mbar_drain(&kfull[i & 1], (uint32_t)(i >> 1) & 1u);
+                for (int i = (vl > 2 ? vl - 2 : 0); i < vl; ++i) mt_mbar_drain(&vfull[i & 1], (uint32_t)(i >> 1) & 1u);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc_s = mt_idesc_tf32(128, 64, false, false);
-            constexpr uint32_t idesc_o = mt_idesc_tf32(128, 64, false, true);
-            bool ok = mt_mbar_wait(qconv, 0, abort_flag, status, 2);
-            auto issue_qk = [&](int i) -> bool {
-                const int s = i & 1;
-                if (i >= 2 && !mt_mbar_wait(&sempty[s], (uint32_t)((i >> 1) - 1) & 1u, abort_flag, status, 2))
-                    return false;
-                if (!mt_mbar_wait(&kconv[s], (uint32_t)(i >> 1) & 1u, abort_flag, status, 2)) return false;
-                mt_tc_fence_after();
-                const uint32_t d = tmem + SC + 64u * (uint32_t)s;
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const uint32_t kh = mt_smem_u32(Khi(s) + j * 2048), kl = mt_smem_u32(Klo(s) + j * 2048);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t ah = tmem + QC + 64u * (uint32_t)j + 8u * (uint32_t)kk;
-                        const uint64_t bh = mt_operand_desc_k(kh, kk), bl = mt_operand_desc_k(kl, kk);
-                        mt_mma_tf32_ts(d, ah, bl, idesc_s, (j | kk) ? 1u : 0u);
-                        mt_mma_tf32_ts(d, ah + 32u, bh, idesc_s, 1u);
-                        mt_mma_tf32_ts(d, ah, bh, idesc_s, 1u);
-                    }
-                }
-                mt_mma_commit(&kempty[s]);
-                mt_mma_commit(&sfull[s]);
-                return true;
-            };
-            if (ok) ok = issue_qk(0);
-            if (ok && nb > 1) ok = issue_qk(1);
+            bool ok = true;
             for (int i = 0; i < nb && ok; ++i) {
                 const int s = i & 1;
                 // pfull(i) also means the softmax threads have folded P V of block i - 2
@@ -185,7 +221,7 @@ __device__ __forceinline__ void mt_attn_fwd_tc(const mt_tmap* tmQ, const mt_tmap
                 }
                 mt_mma_commit(&vempty[s]);
                 mt_mma_commit(pempty);
-                if (i + 2 < nb) ok = issue_qk(i + 2);
+                mt_mbar_arrive(&pvi[s]);
             }
             // All issued MMAs complete before TMEM can be released (bounded).
             mt_mma_commit(mdone);
