@@ -3,7 +3,7 @@
 // "TS", B from shared memory) and timing them with clock64 and CUDA events. Variants:
 // zero or random operand data, and the 3xTF32 pattern (per 8-deep k step three MMAs
 // over A hi / lo and B hi / lo: hi*lo, lo*hi, hi*hi, as the GEMM kernels issue them).
-// Gives the tensor-pipe ceiling the 3xTF32 kernels are judged against (three MMAs per
+// Gives the tensor-pipe ceiling the 3xTF32 kernels are measured against (three MMAs per
 // 8-deep k step). Build and run:
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -o mma_peak metellus_b200/csrc/mma_peak.cu && ./mma_peak
 // The completion wait is bounded (the kernel reports -1 cycles if it gives up).
