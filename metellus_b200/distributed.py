@@ -104,3 +104,25 @@ def combining(*names: str):
 
 def combined_outputs() -> frozenset[str]:
     return _combined.get()
+
+
+def agree(problem: str | None, what: str, group=None) -> None:
+    """Raise ``ValueError`` on every rank if any rank reports a problem.
+
+    Called while planning a step that ends in a collective: a rank that raised alone
+    would leave the others waiting in that collective. The verdicts travel over the
+    host process group (``torch.distributed``); without one (a single process) the
+    local verdict decides."""
+    problems = [problem]
+    try:
+        import torch.distributed as dist
+
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+            problems = [None] * dist.get_world_size(group)
+            dist.all_gather_object(problems, problem, group=group)
+    except ImportError:
+        pass
+    bad = [(r, p) for r, p in enumerate(problems) if p]
+    if bad:
+        r, p = bad[0]
+        raise ValueError(f"{what}: rank {r} cannot take part: {p}" if len(problems) > 1 else p)

@@ -38,19 +38,19 @@ def assemble_split_reduction(decision: DecisionView, function_name: str | None) 
 
     anchor = decision.anchor
     combine = anchor.out.name in distributed.combined_outputs()
+    if combine:
+        # Every rank plans the same program on its own shard; they must all accept or
+        # all reject the combine, or the accepting ranks would wait in the all-reduce
+        # for ranks that raised. So each rank checks its shard and the verdicts are
+        # exchanged on the host before anything is launched.
+        problem = _combine_problem(decision)
+        distributed.agree(problem, what=f"combined reduction {anchor.out.name!r}")
+        return _combined_reduction(decision, function_name, anchor.input, *anchor.input.shape)
     if decision.strategy is not FusionStrategy.STANDALONE_REDUCTION or len(anchor.input.shape) != 2:
-        if combine:
-            raise ValueError(f"reduction {anchor.out.name!r} is combined across GPUs, so it must be a standalone "
-                             "2-D reduction (no fused prologue / epilogue)")
         return None
     src = anchor.input
     M, K = src.shape
     layout_ok = src.col_stride == 1 and (M == 1 or src.row_stride >= K)
-    if combine:
-        if not layout_ok or M > SPLIT_MAX_ROWS:
-            raise ValueError(f"reduction {anchor.out.name!r} is combined across GPUs but its input is not a "
-                             f"row-major matrix of at most {SPLIT_MAX_ROWS} rows")
-        return _combined_reduction(decision, function_name, src, M, K)
     if M > SPLIT_MAX_ROWS or K < SPLIT_MIN_COLS or not layout_ok:
         return None
     ld = src.row_stride if M > 1 else K
@@ -64,6 +64,30 @@ def assemble_split_reduction(decision: DecisionView, function_name: str | None) 
 
 
 PARTIAL_KEY = "__mt_partial64"
+
+
+def _combine_problem(decision: DecisionView) -> str | None:
+    """Why this rank cannot combine the reduction across GPUs (None when it can).
+
+    Only whole-tensor reductions combine: the input must be one row (``sum(X)`` is
+    planned over the (1, M*K) view of the rank's rows). Per-row partials of several
+    rows cannot be added element-wise across ranks, because row i of one rank's
+    shard and row i of another's are different rows of the full tensor."""
+    anchor = decision.anchor
+    name = anchor.out.name
+    if decision.strategy is not FusionStrategy.STANDALONE_REDUCTION or len(anchor.input.shape) != 2:
+        return (f"reduction {name!r} is combined across GPUs, so it must be a standalone 2-D reduction "
+                "(no fused prologue / epilogue)")
+    src = anchor.input
+    M, K = src.shape
+    if M != 1:
+        return (f"reduction {name!r} is combined across GPUs, so it must reduce the whole tensor: its input "
+                f"must be a single row (view the shard as (1, M*K)), not {M} rows")
+    if K < 1:
+        return f"reduction {name!r} is combined across GPUs but this rank's shard is empty"
+    if src.col_stride != 1:
+        return f"reduction {name!r} is combined across GPUs but its input row is not contiguous"
+    return None
 
 
 def _combined_reduction(decision: DecisionView, function_name: str | None, src, M: int, K: int) -> KernelGroup:

@@ -76,3 +76,52 @@ def test_combined_reduction_must_be_standalone():
     ops.reduction("sum", out="S", x="E", axis=-1)
     with distributed.combining("S"), pytest.raises(ValueError, match="combined across GPUs"):
         compile_program(ops)
+
+
+def test_combined_reduction_rejects_several_rows():
+    """Per-row partials of a row-sharded tensor cannot be combined element-wise
+    (row i of two shards are different rows), so only whole-tensor reductions combine."""
+    from metellus_b200 import Operations
+
+    ops = Operations()
+    ops.input("X", (4, 1 << 16))
+    ops.reduction("sum", out="S", x="X", axis=-1)
+    with distributed.combining("S"), pytest.raises(ValueError, match="single row"):
+        compile_program(ops)
+
+
+def _agree_rank(rank: int, world: int, port: int, q) -> None:
+    """Rank 1 holds a shard that cannot be combined (4 rows); rank 0's is fine. Both
+    must raise while planning, before any collective would be launched."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from metellus_b200 import Operations
+
+    try:
+        ops = Operations()
+        ops.input("X", (1, 1 << 16) if rank == 0 else (4, 1 << 14))
+        ops.reduction("sum", out="S", x="X", axis=-1)
+        try:
+            with distributed.combining("S"):
+                compile_program(ops)
+            q.put((rank, "planned"))
+        except ValueError as e:
+            q.put((rank, str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_combined_reduction_all_ranks_reject_together():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_agree_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert "rank 1 cannot take part" in got[0], got
+    assert "rank 1 cannot take part" in got[1], got

@@ -1,7 +1,7 @@
-"""Sharded whole-tensor sum on two GPUs: each rank reduces its shard of X to an fp64
+"""Sharded whole-tensor sum on 2, 4 and 8 GPUs (as many as the box has): each rank reduces its shard of X to an fp64
 partial and one NCCL all-reduce combines them (``distributed.combining``). Both ranks
-must return the fp64 sum of the full (two-shard) tensor rounded once. Runs as two
-child processes, one per GPU; skipped with fewer than two GPUs."""
+must return the fp64 sum of the full tensor rounded once. Runs as child processes,
+one per GPU; a world size larger than the box's GPU count is skipped."""
 
 from __future__ import annotations
 
@@ -36,11 +36,12 @@ def _rank(rank: int, world: int, port: int, q) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sharded_sum_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_sum(world):
     from metellus_b200 import configs
 
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 1000

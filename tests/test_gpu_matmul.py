@@ -128,7 +128,7 @@ def test_dual_gemm_epilogue(cuda_device, M, K, N, tb):
     assert_matmul_close(res.env["U"], r64["U"], r32["U"], what=f"dual {M}x{K}x{N} tb={tb}")
 
 
-@pytest.mark.parametrize("K", [2048, 4096])
+@pytest.mark.parametrize("K", [2048, 4096, 8192])
 def test_tc_matmul_long_k(cuda_device, K):
     """Long reductions: the per-32 chunk promotion keeps the error at fp32-dot level."""
     ops, out = _mm(256, K, 256, seed=K)
