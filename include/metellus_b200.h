@@ -135,8 +135,11 @@ int mt_reduce_rows(int dev, uint64_t in_buf, uint64_t out_buf, uint64_t rows, ui
  * (rows * splits * 8 + rows * 4 > 256 KiB, splits ~ 8 blocks per SM / rows: a few-row
  * reduction needs ~10 KB; one-split plans fit up to 21,845 rows).
  * The first call on a device looks up the array's device address (module set-up):
- * make it before any stream capture. All calls share the array, so calls that
- * overlap on the GPU (different streams) race; the tickets are cleared per call. */
+ * make it before any stream capture. That address is kept for the life of the
+ * process, so do not call cudaDeviceReset between calls. All calls share the array,
+ * so calls that overlap on the GPU (different streams) race; the tickets are cleared
+ * per call. A caller's stream must belong to `dev`; the caller's current device is
+ * restored before returning. */
 int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, uint64_t cols, uint64_t ld,
                            int op, void* stream);
 

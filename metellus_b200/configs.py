@@ -241,3 +241,37 @@ def algorithmic_work(key: str, **shape) -> tuple[float, float]:
         M, D, F = s["M"], s["D"], s["F"]
         return 3 * 2.0 * M * D * F, 4.0 * (2 * M * D + 3 * D * F + F + D)
     raise KeyError(key)
+
+
+SHARD_AXIS = {"c1": None, "c2": "M", "c3": "M", "c3sum": "M", "c4": "B", "c5": "M"}
+
+
+def shard(key: str, world: int, rank: int, seed: int = 0, **shape) -> tuple[Operations, dict]:
+    """Rank ``rank``'s part of config ``key`` split ``world`` ways (strong scaling).
+
+    The full configuration's inputs are drawn (seeded, identical on every rank) and the
+    program is rebuilt on this rank's contiguous block of rows (C2, C3, C3-sum, C5) or
+    heads (C4); weights (C5's W1, W3, W2 and biases) are replicated. C1 has no batch or
+    row dimension to split (its 1024 rows are one GEMM), so every rank runs the whole
+    program (replicas). Returns (ops, this rank's shape)."""
+    from metellus_b200.distributed import row_range
+
+    c = CONFIGS[key]
+    full = {**c.full, **shape}
+    axis = SHARD_AXIS[key]
+    if axis is None or world == 1:
+        return c.build(**full, seed=seed), full
+    a, b = row_range(full[axis], rank, world)
+    u = c.build(**full, seed=seed).uploads
+    local = {**full, axis: b - a}
+    if key == "c2":
+        return elementwise_dag_ops(u["x"][a:b], u["y"][a:b], u["z"][a:b]), local
+    if key == "c3":
+        return row_softmax(X=u["X"][a:b]), local
+    if key == "c3sum":
+        return tensor_sum(X=u["X"][a:b]), local
+    if key == "c4":
+        return attention_ops(u["Q"][a:b], u["K"][a:b], u["V"][a:b]), local
+    if key == "c5":
+        return mlp_ops(u["X"][a:b], u["W1"], u["W3"], u["W2"], u["b1"], u["b2"]), local
+    raise KeyError(key)

@@ -47,18 +47,6 @@ def build_backend(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
-def build_mma_peak(force: bool = False) -> Path:
-    """The tcgen05 tf32 issue-rate microbenchmark (``mma_peak.cu``) as an executable
-    next to the library."""
-    src = PKG / "csrc" / "mma_peak.cu"
-    exe = LIB_DIR / "mma_peak"
-    LIB_DIR.mkdir(exist_ok=True)
-    if not force and exe.exists() and exe.stat().st_mtime >= src.stat().st_mtime:
-        return exe
-    subprocess.run([nvcc(), *ARCH_FLAGS, "-O3", "-o", str(exe), str(src)], check=True)
-    return exe
-
-
 if __name__ == "__main__":
     build_backend(force="--force" in sys.argv, verbose=True)
     print(LIB)

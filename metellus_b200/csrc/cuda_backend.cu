@@ -696,7 +696,20 @@ int mt_reduce_rows_noalloc(int dev, const float* in, float* out, uint64_t rows, 
             return fail("mt_reduce_rows_noalloc: no stream given and device %d not initialised "
                         "(pass a stream or call mt_init first)", dev);
         st = g_dev[dev].stream;
+    } else {
+        int sdev = -1;
+        RT_CHECK(cudaStreamGetDevice(st, &sdev));
+        if (sdev != dev)
+            return fail("mt_reduce_rows_noalloc: the stream belongs to device %d, not device %d", sdev, dev);
     }
+    // The caller (often another framework) keeps its own current device: switch to
+    // `dev` for the set-up and the launch and switch back on every return path.
+    int caller_dev = -1;
+    RT_CHECK(cudaGetDevice(&caller_dev));
+    struct RestoreDevice {
+        int d;
+        ~RestoreDevice() { if (d >= 0) cudaSetDevice(d); }
+    } restore{caller_dev};
     RT_CHECK(cudaSetDevice(dev));
     int sms = 148;
     RT_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

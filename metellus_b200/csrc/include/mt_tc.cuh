@@ -14,7 +14,14 @@
 // word after the launch and raises.
 #pragma once
 
+// The limit can be set before this header (a test shortens it to exercise the
+// timeout path on a kernel whose producer is told to stop early, below).
+#ifndef MT_WAIT_LIMIT_NS
 #define MT_WAIT_LIMIT_NS 2000000000ull  // 2 s per wait
+#endif
+// MT_TEST_STALL_KTILE (test builds only, never defined by the planner): the TMA
+// producer stops before that k-tile, so the consumers' bounded waits run out and the
+// kernel takes its abort path (status word, drained copies, TMEM freed, return).
 
 struct alignas(64) mt_tmap { unsigned long long v[16]; };
 
@@ -691,6 +698,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
                 const int r = kt % RST;
                 if (kt >= RST && !mt_mbar_wait(&rempty[r], (uint32_t)((kt / RST) - 1) & 1u, abort_flag, status, 1))
                     break;
+#ifdef MT_TEST_STALL_KTILE
+                if (kt == MT_TEST_STALL_KTILE) break;
+#endif
                 mt_mbar_expect_tx(&rfull[r], L::kRawBytes);
                 const int kg = (kbeg + kt) * 32;
                 mt_tma_load_2d(A_raw(r), tmA, &rfull[r], kg, m0);
