@@ -1,11 +1,29 @@
-"""``Operations``: the name-resolution builder for the IR (builder.py:50-333).
+"""``Operations``: the user-facing program builder (reference API:
+src/orchestrator/builder.py:50-333).
 
-Callers name tensors by string; the builder keeps a name -> Tensor registry, records
-numpy uploads, and appends validated ops. Views (transpose / metadata reshape) are
-registry entries, not ops; a reshape that cannot be a view becomes a ``ShapeOp``.
+A program is written against tensor *names*. The builder keeps one record per name
+(its ``Tensor``: shape, strides, storage owner), the host arrays to upload, and the
+ordered list of IR ops. Three kinds of call:
+
+* declarations — ``input`` (shape only) and ``from_numpy`` (shape + payload);
+* ops — ``matmul``, ``elementwise``, ``reduction`` and the copying ``reshape``;
+  each creates exactly one new name (the IR is SSA), and the op's own constructor
+  does the shape / broadcast / dtype validation;
+* views — ``transpose`` and the metadata ``reshape``: a new name over the same
+  storage, no op.
+
+A failed op leaves the builder unchanged: the output name is registered only after
+the op has been constructed. ``build()`` returns a copy of the op list, so the
+builder can keep growing afterwards.
+
+Batched (rank-3) tensors are accepted everywhere the IR accepts them; ``matmul``
+infers ``a.shape[:-1] + (b.shape[-1],)`` as its output shape.
 """
 
 from __future__ import annotations
+
+import math
+from typing import Callable
 
 import numpy as np
 
@@ -14,6 +32,7 @@ from metellus_b200.orchestrator.ir import (
     ElementwiseOp,
     Layout,
     MatmulOp,
+    Op,
     OperandValue,
     Program,
     ReductionOp,
@@ -23,220 +42,171 @@ from metellus_b200.orchestrator.ir import (
 )
 
 
+def addressable_elements(t: Tensor) -> int:
+    """How many elements of backing storage ``t`` can touch: one past the largest
+    offset it addresses (``1`` for a scalar)."""
+    strides = {0: (), 1: (t.row_stride,), 2: (t.row_stride, t.col_stride),
+               3: (t.batch_stride, t.row_stride, t.col_stride)}[len(t.shape)]
+    return 1 + sum((extent - 1) * stride for extent, stride in zip(t.shape, strides))
+
+
 class Operations:
-    """Mutable program builder. ``build()`` returns a fresh op-list snapshot."""
+    """Builder for one program (mutable; ``build()`` snapshots the op list)."""
 
     def __init__(self, dtype: str = "float32") -> None:
         self._dtype = dtype
-        self._tensors: dict[str, Tensor] = {}
-        self._ops: Program = []
-        self._uploads: dict[str, np.ndarray] = {}
+        self._by_name: dict[str, Tensor] = {}
+        self._program: Program = []
+        self._payloads: dict[str, np.ndarray] = {}
 
-    # -- tensor registry -----------------------------------------------------
+    # -- lookups --------------------------------------------------------------
 
-    def input(
-        self,
-        name: str,
-        shape: tuple[int, ...],
-        layout: Layout = Layout.ROW_MAJOR,
-        row_stride: int | None = None,
-        col_stride: int | None = None,
-    ) -> Tensor:
-        """Declare a caller-supplied tensor (builder.py:62-79)."""
-        return self._declare(name, shape, layout=layout, row_stride=row_stride,
-                             col_stride=col_stride)
+    def _lookup(self, name: str) -> Tensor:
+        try:
+            return self._by_name[name]
+        except KeyError:
+            raise ValueError(f"tensor {name!r} is not declared: declare it with input() / from_numpy() "
+                             "or produce it with an op first") from None
+
+    def _require_fresh_view_name(self, out: str, what: str) -> None:
+        if out in self._by_name:
+            raise ValueError(f"{what} output {out!r} already declared; views need a new name")
+
+    def _emit(self, out: str, shape: tuple[int, ...], make: Callable[[Tensor], Op]) -> Tensor:
+        """Create op ``make(out_tensor)`` writing the new name ``out``; register the
+        name and append the op only when construction (= validation) succeeded."""
+        if out in self._by_name:
+            raise ValueError(f"output tensor {out!r} already exists; the IR is SSA, so every op "
+                             "needs a new output name")
+        result = Tensor(name=out, shape=tuple(shape), dtype=self._dtype)
+        op = make(result)
+        self._by_name[out] = result
+        self._program.append(op)
+        return result
+
+    # -- declarations ------------------------------------------------------------
+
+    def input(self, name: str, shape: tuple[int, ...], layout: Layout = Layout.ROW_MAJOR,
+              row_stride: int | None = None, col_stride: int | None = None) -> Tensor:
+        """Declare a tensor the caller supplies (no producing op). Strides default to
+        the contiguous ones for ``layout``. Re-declaring a name with the same shape
+        returns the existing tensor; with another shape it is an error."""
+        shape = tuple(shape)
+        known = self._by_name.get(name)
+        if known is not None:
+            if known.shape != shape:
+                raise ValueError(f"tensor {name!r} already declared with shape {known.shape}; "
+                                 f"cannot declare it again as {shape}")
+            return known
+        t = Tensor(name=name, shape=shape, dtype=self._dtype, layout=layout,
+                   row_stride=-1 if row_stride is None else row_stride,
+                   col_stride=-1 if col_stride is None else col_stride)
+        self._by_name[name] = t
+        return t
 
     def from_numpy(self, arr: np.ndarray, name: str) -> Tensor:
-        """Declare an input and record its payload (builder.py:81-114). Only float32
-        storage owners are accepted."""
+        """Declare ``name`` with ``arr``'s shape and record ``arr`` as its upload.
+        The array must be float32 (no silent widening or narrowing), ``name`` must
+        own its storage (not a view), and the array must hold every element the
+        tensor's strides can reach."""
         if arr.dtype != np.float32:
-            raise ValueError(f"from_numpy: array dtype must be float32; got {arr.dtype}")
-        t = self._declare(name, tuple(arr.shape))
+            raise ValueError(f"from_numpy({name!r}): the array must be float32, got {arr.dtype}")
+        t = self.input(name, tuple(arr.shape))
         if t.buffer_key != name:
-            raise ValueError(
-                f"from_numpy: {name!r} is a view of {t.buffer_key!r}; only "
-                "storage owners can be uploaded"
-            )
+            raise ValueError(f"from_numpy: {name!r} is a view of {t.buffer_key!r}; only a storage owner "
+                             "can receive an upload")
         if tuple(arr.shape) != t.shape:
-            raise ValueError(
-                f"from_numpy: array shape {tuple(arr.shape)} does not match "
-                f"declared tensor shape {t.shape}"
-            )
-        required = _required_storage_elements(t)
-        if arr.size < required:
-            raise ValueError(
-                f"from_numpy: array with shape {tuple(arr.shape)} provides {arr.size} "
-                f"elements, but tensor {name!r} with strides (row_stride={t.row_stride}, "
-                f"col_stride={t.col_stride}) can address {required} elements"
-            )
-        self._uploads[name] = arr
+            raise ValueError(f"from_numpy({name!r}): array shape {tuple(arr.shape)} differs from the "
+                             f"declared shape {t.shape}")
+        reach = addressable_elements(t)
+        if arr.size < reach:
+            raise ValueError(f"from_numpy({name!r}): the array has {arr.size} elements, but with "
+                             f"row_stride={t.row_stride}, col_stride={t.col_stride} the tensor can address "
+                             f"{reach} elements")
+        self._payloads[name] = arr
         return t
-
-    def _declare(
-        self,
-        name: str,
-        shape: tuple[int, ...],
-        *,
-        layout: Layout = Layout.ROW_MAJOR,
-        row_stride: int | None = None,
-        col_stride: int | None = None,
-    ) -> Tensor:
-        existing = self._tensors.get(name)
-        if existing is not None:
-            if existing.shape != tuple(shape):
-                raise ValueError(
-                    f"tensor {name!r} already declared with shape {existing.shape}, "
-                    f"cannot redeclare as {tuple(shape)}"
-                )
-            return existing
-        t = Tensor(
-            name=name,
-            shape=tuple(shape),
-            dtype=self._dtype,
-            layout=layout,
-            row_stride=-1 if row_stride is None else row_stride,
-            col_stride=-1 if col_stride is None else col_stride,
-        )
-        self._tensors[name] = t
-        return t
-
-    def _bind_existing(self, name: str) -> Tensor:
-        t = self._tensors.get(name)
-        if t is None:
-            raise ValueError(
-                f"tensor {name!r} is not declared — call ops.input(...) first "
-                "or use an op that produces it"
-            )
-        return t
-
-    def _reserve_output(self, name: str, shape: tuple[int, ...]) -> Tensor:
-        if name in self._tensors:
-            raise ValueError(f"output tensor {name!r} already defined; IR is SSA — pick a fresh name")
-        return Tensor(name=name, shape=tuple(shape), dtype=self._dtype)
-
-    def _commit_output(self, t: Tensor) -> None:
-        self._tensors[t.name] = t
 
     # -- ops -------------------------------------------------------------------
 
     def matmul(self, a: str, b: str, out: str) -> Tensor:
-        a_t = self._bind_existing(a)
-        b_t = self._bind_existing(b)
-        out_t = self._reserve_output(out, a_t.shape[:-1] + (b_t.shape[-1],))
-        op = MatmulOp(out=out_t, a=a_t, b=b_t)
-        self._commit_output(out_t)
-        self._ops.append(op)
-        return out_t
+        """``out = a @ b`` (per batch index for rank-3 operands)."""
+        ta, tb = self._lookup(a), self._lookup(b)
+        return self._emit(out, ta.shape[:-1] + tb.shape[-1:], lambda o: MatmulOp(out=o, a=ta, b=tb))
 
-    def elementwise(
-        self,
-        op: str,
-        out: str,
-        operands: tuple[str | int | float, ...],
-        y_broadcast: BroadcastSpec | str = BroadcastSpec.NONE,
-        cond_broadcast: BroadcastSpec | str = BroadcastSpec.NONE,
-    ) -> Tensor:
-        """Pointwise op; numeric literals become ``Scalar`` operands (builder.py:183-235)."""
-        y_bc = BroadcastSpec(y_broadcast)
-        cond_bc = BroadcastSpec(cond_broadcast)
-        resolved: list[OperandValue] = []
-        for o in operands:
-            if isinstance(o, str):
-                resolved.append(self._bind_existing(o))
-            elif isinstance(o, (int, float)) and not isinstance(o, bool):
-                resolved.append(Scalar(value=float(o)))
-            else:
-                raise ValueError(
-                    f"operand {o!r} must be a tensor name (str) or numeric literal (int/float)"
-                )
-        primary = resolved[0] if resolved else None
-        if not isinstance(primary, Tensor):
-            raise ValueError(
-                f"elementwise {op!r}: operand[0] must be a tensor name; got "
-                f"{operands[0] if operands else None!r}. Scalars are only allowed as "
-                "secondary operands."
-            )
-        out_t = self._reserve_output(out, primary.shape)
-        ew = ElementwiseOp(out=out_t, op=op, operands=tuple(resolved), y_broadcast=y_bc,
-                           cond_broadcast=cond_bc)
-        self._commit_output(out_t)
-        self._ops.append(ew)
-        return out_t
+    def elementwise(self, op: str, out: str, operands: tuple[str | int | float, ...],
+                    y_broadcast: BroadcastSpec | str = BroadcastSpec.NONE,
+                    cond_broadcast: BroadcastSpec | str = BroadcastSpec.NONE) -> Tensor:
+        """Pointwise ``op``; the output has the first operand's shape. Operands are
+        declared tensor names or Python numbers (inlined as ``Scalar`` constants);
+        the first must be a tensor."""
+        y_mode, cond_mode = BroadcastSpec(y_broadcast), BroadcastSpec(cond_broadcast)
+        values: list[OperandValue] = [self._operand(o) for o in operands]
+        if not values or not isinstance(values[0], Tensor):
+            first = operands[0] if operands else None
+            raise ValueError(f"elementwise {op!r}: operand[0] must be a tensor name, got {first!r}; "
+                             "numbers may only be secondary operands")
+        return self._emit(out, values[0].shape,
+                          lambda o: ElementwiseOp(out=o, op=op, operands=tuple(values), y_broadcast=y_mode,
+                                                  cond_broadcast=cond_mode))
 
-    def transpose(self, name: str, out: str) -> Tensor:
-        """Logical transpose view; no op is emitted (builder.py:237-249)."""
-        src = self._bind_existing(name)
-        if out in self._tensors:
-            raise ValueError(f"view tensor {out!r} already declared; pick a fresh name")
-        view = src.transpose(out)
-        self._tensors[out] = view
-        return view
-
-    def reshape(self, name: str, new_shape: tuple[int, ...], out: str) -> Tensor:
-        """Metadata view when possible, ``ShapeOp`` copy otherwise (builder.py:251-294)."""
-        src = self._bind_existing(name)
-        if out in self._tensors:
-            raise ValueError(f"reshape output {out!r} already declared; pick a fresh name")
-        new_shape_t = tuple(new_shape)
-        if src.can_reshape_as_view(new_shape_t):
-            view = src.reshape_view(new_shape_t, out)
-            self._tensors[out] = view
-            return view
-        if len(new_shape_t) == 0 or len(new_shape_t) > 2:
-            raise ValueError(f"reshape target rank must be 1D or 2D; got {new_shape_t}")
-        prod = 1
-        for d in new_shape_t:
-            prod *= d
-        if prod != src.element_count:
-            raise ValueError(
-                f"reshape element-count mismatch: {src.shape} ({src.element_count}) -> "
-                f"{new_shape_t} ({prod})"
-            )
-        out_t = self._reserve_output(out, new_shape_t)
-        op = ShapeOp(out=out_t, input=src)
-        self._commit_output(out_t)
-        self._ops.append(op)
-        return out_t
+    def _operand(self, o: str | int | float) -> OperandValue:
+        if isinstance(o, str):
+            return self._lookup(o)
+        if isinstance(o, (int, float)) and not isinstance(o, bool):
+            return Scalar(value=float(o))
+        raise ValueError(f"operand {o!r} must be a tensor name (str) or a numeric literal (int / float)")
 
     def reduction(self, op: str, out: str, x: str, axis: int = -1) -> Tensor:
-        """Last-axis reduction (builder.py:296-317)."""
+        """Reduce ``x`` along ``axis`` (the IR accepts the last axis only)."""
         from metellus_b200.compute.reduction import REDUCTION_OPS
 
         if op not in REDUCTION_OPS:
-            raise ValueError(f"reduction op {op!r} not in {REDUCTION_OPS}")
-        x_t = self._bind_existing(x)
-        normalized = axis if axis >= 0 else len(x_t.shape) + axis
-        if 0 <= normalized < len(x_t.shape):
-            out_shape = x_t.shape[:normalized] + x_t.shape[normalized + 1 :]
-        else:
-            out_shape = x_t.shape[:-1] or (1,)
-        out_t = self._reserve_output(out, out_shape)
-        red = ReductionOp(out=out_t, op=op, input=x_t, axis=axis)
-        self._commit_output(out_t)
-        self._ops.append(red)
-        return out_t
+            raise ValueError(f"reduction op {op!r} is not one of {REDUCTION_OPS}")
+        src = self._lookup(x)
+        rank = len(src.shape)
+        ax = axis + rank if axis < 0 else axis
+        # the dropped axis, or (for an invalid axis) the last one, so that the IR op
+        # reports the real problem
+        keep = [d for i, d in enumerate(src.shape) if i != (ax if 0 <= ax < rank else rank - 1)]
+        shape = tuple(keep) or (1,)
+        return self._emit(out, shape, lambda o: ReductionOp(out=o, op=op, input=src, axis=axis))
 
-    # -- finalize ----------------------------------------------------------------
+    # -- views -----------------------------------------------------------------
+
+    def transpose(self, name: str, out: str) -> Tensor:
+        """``out`` = the transpose of ``name``'s (inner) matrix as a view: same storage,
+        swapped shape and strides, no op."""
+        src = self._lookup(name)
+        self._require_fresh_view_name(out, "transpose")
+        self._by_name[out] = view = src.transpose(out)
+        return view
+
+    def reshape(self, name: str, new_shape: tuple[int, ...], out: str) -> Tensor:
+        """A metadata view when the source can be walked linearly (same storage, no
+        op); otherwise a ``ShapeOp`` that gathers the source into a new contiguous
+        1-D or 2-D tensor."""
+        src = self._lookup(name)
+        self._require_fresh_view_name(out, "reshape")
+        target = tuple(new_shape)
+        if src.can_reshape_as_view(target):
+            self._by_name[out] = view = src.reshape_view(target, out)
+            return view
+        if not 1 <= len(target) <= 2:
+            raise ValueError(f"a copying reshape needs a 1D or 2D target rank; got {target}")
+        if math.prod(target) != src.element_count:
+            raise ValueError(f"reshape element-count mismatch: {src.shape} has {src.element_count} elements, "
+                             f"{target} has {math.prod(target)}")
+        return self._emit(out, target, lambda o: ShapeOp(out=o, input=src))
+
+    # -- results ---------------------------------------------------------------
 
     def build(self) -> Program:
-        return list(self._ops)
+        return list(self._program)
 
     @property
     def tensors(self) -> dict[str, Tensor]:
-        return dict(self._tensors)
+        return dict(self._by_name)
 
     @property
     def uploads(self) -> dict[str, np.ndarray]:
-        return dict(self._uploads)
-
-
-def _required_storage_elements(t: Tensor) -> int:
-    if len(t.shape) == 0:
-        return 1
-    if len(t.shape) == 1:
-        return (t.shape[0] - 1) * t.row_stride + 1
-    if len(t.shape) == 2:
-        rows, cols = t.shape
-        return (rows - 1) * t.row_stride + (cols - 1) * t.col_stride + 1
-    b, rows, cols = t.shape
-    return (b - 1) * t.batch_stride + (rows - 1) * t.row_stride + (cols - 1) * t.col_stride + 1
+        return dict(self._payloads)

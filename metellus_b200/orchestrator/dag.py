@@ -1,10 +1,14 @@
-"""Producer / consumer view over an IR program (dag.py:46-76): validates SSA and
-def-before-use, and exposes program inputs (read, never produced) and outputs
-(produced, never read)."""
+"""Producer / consumer index of an IR program (reference API: src/orchestrator/dag.py).
+
+``build_dag`` walks the ops once, in program order, and checks the two rules the
+rest of the compiler relies on: every tensor name is written by at most one op
+(SSA), and no op writes a name that an earlier op already read (the program is in
+topological order). It records who writes and who reads each name; program inputs
+are the names read but never written, outputs the names written but never read.
+"""
 
 from __future__ import annotations
 
-from collections import defaultdict
 from dataclasses import dataclass
 
 from metellus_b200.orchestrator.ir import Op, Program
@@ -19,35 +23,28 @@ class DAG:
     outputs: frozenset[str]
 
     def unique_consumer(self, name: str) -> Op | None:
-        cs = self.consumers_of.get(name, ())
-        return cs[0] if len(cs) == 1 else None
+        """The only op reading ``name``, or None when zero or several ops read it."""
+        readers = self.consumers_of.get(name, ())
+        return readers[0] if len(readers) == 1 else None
 
     def topo_order(self) -> list[Op]:
         return list(self.program)
 
 
 def build_dag(program: Program) -> DAG:
-    producer_of: dict[str, Op] = {}
-    consumer_lists: dict[str, list[Op]] = defaultdict(list)
-    used: set[str] = set()
+    writer: dict[str, Op] = {}
+    readers: dict[str, list[Op]] = {}
     for op in program:
         for t in op.inputs:
-            consumer_lists[t.name].append(op)
-            used.add(t.name)
-        out_name = op.out.name
-        if out_name in producer_of:
-            raise ValueError(f"SSA violation: tensor {out_name!r} produced by two ops")
-        if out_name in used:
-            raise ValueError(
-                f"def-after-use: tensor {out_name!r} consumed before it is defined "
-                "(program must be in topological order)"
-            )
-        producer_of[out_name] = op
-    produced = set(producer_of)
-    return DAG(
-        program=list(program),
-        producer_of=producer_of,
-        consumers_of={n: tuple(v) for n, v in consumer_lists.items()},
-        inputs=frozenset(used - produced),
-        outputs=frozenset(produced - used),
-    )
+            readers.setdefault(t.name, []).append(op)
+        name = op.out.name
+        if name in writer:
+            raise ValueError(f"SSA violation: {name!r} is written by two ops")
+        if name in readers:
+            raise ValueError(f"def-after-use: {name!r} is read before the op that writes it "
+                             "(ops must be listed in topological order)")
+        writer[name] = op
+    read, written = set(readers), set(writer)
+    return DAG(program=list(program), producer_of=writer,
+               consumers_of={n: tuple(ops) for n, ops in readers.items()},
+               inputs=frozenset(read - written), outputs=frozenset(written - read))
