@@ -311,6 +311,13 @@ __device__ __forceinline__ void mt_tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+template <int W>
+__device__ __forceinline__ void mt_tmem_ldw(uint32_t taddr, float (&v)[W]) {
+    static_assert(W == 16 || W == 32, "16- or 32-column loads");
+    if constexpr (W == 32) mt_tmem_ld32(taddr, v);
+    else mt_tmem_ld16(taddr, v);
+}
+
 __device__ __forceinline__ void mt_tmem_st16(uint32_t taddr, const float* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -884,6 +891,11 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 #endif
 
 // ---------------------------------------------------------------------------------
+// Columns per tensor-memory load when the accumulator warps drain a chunk buffer.
+#ifndef MT_PAIR_DRAIN_W
+#define MT_PAIR_DRAIN_W 16
+#endif
+
 // CTA-pair GEMM: a 256 x 128 output tile per cluster of two CTAs (cta_group::2).
 //
 // The even CTA (rank 0) issues every MMA for both: M = 256 (its 128 A rows and the
@@ -912,8 +924,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // CTA's tempty; the even CTA's MMA commits arrive on both CTAs' cempty / tfull
 // (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
 // before tensor memory is freed and either exits.
-template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, int NISSUE, class ProA,
-          class ProB, class Epi>
+template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, int NISSUE, bool SACC,
+          class ProA, class ProB, class Epi>
 __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                     int M, int N, int K, const ProA& proA, const ProB& proB,
                                                     const Epi& epi, int* status, void* smem_raw) {
@@ -926,11 +938,14 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     constexpr uint32_t kConvBytes = 2u * kBBytes;
     constexpr uint32_t kConvOffset = RST * kRawBytes;
     constexpr uint32_t kBarOffset = kConvOffset + CST * kConvBytes;
-    constexpr uint32_t ACOLS = (uint32_t)NACC * NMMA;  // NACC chunk buffers of accumulators
+    // NACC chunk buffers of accumulators (+ SACC: one buffer of the small products)
+    constexpr uint32_t ACOLS = (uint32_t)(NACC + (SACC ? 1 : 0)) * NMMA;
     static_assert(NMMA == 128, "pair tiles are 256 x 128");
     static_assert(NB * HALF <= 64, "at most 64 accumulator registers per thread");
     static_assert(ACOLS + 64u * CST <= 512, "accumulators and A stages exceed TMEM");
-    static_assert(NISSUE == 1 || (NISSUE == 2 && NACC == 2), "two issuers own one accumulator buffer each");
+    static_assert(SACC ? (NISSUE == 2 && NACC == 1)
+                       : (NISSUE == 1 || (NISSUE == 2 && NACC == 2)),
+                  "two issuers own one accumulator buffer each (SACC: one issues hi*hi, the other the small products)");
     constexpr uint32_t NCOLS = 512;
     constexpr int NCONV = 6;
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -942,7 +957,8 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     uint64_t* tfull = cempty + CST;     // [NACC] both CTAs: rank 0's MMA commit
     uint64_t* tempty = tfull + NACC;    // [NACC] used on rank 0: both CTAs' accumulator warps
     uint64_t* mdone = tempty + NACC;    // [2] rank 0: each issuer's MMAs drained on the abort path
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 2);
+    uint64_t* sdone = mdone + 2;        // SACC, both CTAs: the small-product issuer's last commit
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sdone + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
@@ -974,7 +990,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         }
         for (int c = 0; c < CST; ++c) {
             mt_mbar_init(&cfull[c], 2 * NCONV);
-            mt_mbar_init(&cempty[c], 1);
+            mt_mbar_init(&cempty[c], SACC ? 2 : 1);   // SACC: both issuers read every stage
         }
         for (int b = 0; b < NACC; ++b) {
             mt_mbar_init(&tfull[b], 1);
@@ -982,6 +998,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         }
         mt_mbar_init(&mdone[0], 1);
         mt_mbar_init(&mdone[1], 1);
+        mt_mbar_init(sdone, 1);
         *abort_flag = 0;
         mt_fence_barrier_init();
     }
@@ -1028,7 +1045,78 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
         // pipe idle for every cycle it spends between two MMAs (measured: an N-cycle
         // gap per 12 MMAs costs ~N cycles of pipe time).
         const int issuer = warp == 1 ? 0 : 1;
-        if (rank == 0 && lane == 0) {
+        if (SACC && rank == 0 && lane == 0) {
+            // SACC: issuer 0 (warp 1) accumulates hi*hi of CHUNK k-tiles at a time into
+            // the one chunk buffer, which the accumulator warps promote into fp32
+            // registers; issuer 1 (warp 0) accumulates the small products hi*lo + lo*hi
+            // of the whole K into their own buffer, read once at the end (they are
+            // ~2^-11 of the result, so the tensor core's accumulation error on them is
+            // negligible). While the chunk buffer drains, issuer 1 keeps the pipe busy.
+            constexpr uint32_t idesc = mt_idesc_tf32(256, NMMA, false, B_MN);
+            bool ok = true;
+            const uint32_t dH = tmem, dS = tmem + (uint32_t)NMMA;
+            if (issuer == 0) {
+                const int nchunks = (nk + CHUNK - 1) / CHUNK;
+                MT_PROF_BEGIN(tloop);
+                for (int ch = 0; ch < nchunks && ok; ++ch) {
+                    MT_PROF_BEGIN(w1);
+                    if (ch >= 1 && !mt_mbar_wait(&tempty[0], (uint32_t)(ch - 1) & 1u, abort_flag, status, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    MT_PROF_END(w1, p_mma_tempty);
+                    const int kt0 = ch * CHUNK, kt1 = min(kt0 + CHUNK, nk);
+                    for (int kt = kt0; kt < kt1; ++kt) {
+                        const int c = kt % CST;
+                        MT_PROF_BEGIN(w2);
+                        if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
+                            ok = false;
+                            break;
+                        }
+                        MT_PROF_END(w2, p_mma_cfull);
+                        mt_tc_fence_after();
+                        const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
+                        const uint32_t bh = mt_smem_u32(B_cv(c, 0));
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
+                            mt_mma_tf32_ts_pair(dH, ah + 8u * (uint32_t)kk, dbh, idesc, (kt != kt0 || kk) ? 1u : 0u);
+                        }
+                        mt_mma_commit_pair_both(&cempty[c]);
+                    }
+                    if (ok) mt_mma_commit_pair_both(&tfull[0]);
+                }
+                MT_PROF_END(tloop, p_mma_loop);
+            } else {
+                for (int kt = 0; kt < nk && ok; ++kt) {
+                    const int c = kt % CST;
+                    MT_PROF_BEGIN(w6);
+                    if (!mt_mbar_wait(&cfull[c], (uint32_t)(kt / CST) & 1u, abort_flag, status, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    MT_PROF_END(w6, p_mma_issue);
+                    mt_tc_fence_after();
+                    const uint32_t ah = tmem + ACOLS + 64u * (uint32_t)c;
+                    const uint32_t bh = mt_smem_u32(B_cv(c, 0)), bl = mt_smem_u32(B_cv(c, 1));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t dah = ah + 8u * (uint32_t)kk;
+                        const uint32_t dal = dah + 32u;
+                        const uint64_t dbh = B_MN ? mt_operand_desc_mn(bh, kk) : mt_operand_desc_k(bh, kk);
+                        const uint64_t dbl = B_MN ? mt_operand_desc_mn(bl, kk) : mt_operand_desc_k(bl, kk);
+                        mt_mma_tf32_ts_pair(dS, dah, dbl, idesc, (kt || kk) ? 1u : 0u);
+                        mt_mma_tf32_ts_pair(dS, dal, dbh, idesc, 1u);
+                    }
+                    mt_mma_commit_pair_both(&cempty[c]);
+                }
+                if (ok) mt_mma_commit_pair_both(sdone);
+            }
+            if (!ok) {  // let the MMAs in flight finish before tensor memory is freed
+                mt_mma_commit_pair_local(&mdone[issuer]);
+                mt_mbar_drain(&mdone[issuer], 0);
+            }
+        } else if (!SACC && rank == 0 && lane == 0) {
             constexpr uint32_t idesc = mt_idesc_tf32(256, NMMA, false, B_MN);
             bool ok = true;
             const int nchunks = (nk + CHUNK - 1) / CHUNK;
@@ -1134,7 +1222,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
             // NB * HALF / 16 loads of 16 columns (544 threads leave 96 registers per
             // thread: 64 accumulators + 16 loaded values); the buffer is released as
             // soon as the last load has landed, before its adds
-            constexpr int W = 16;
+            constexpr int W = MT_PAIR_DRAIN_W;
             constexpr int PER = HALF / W;
             constexpr int NLD = NB * PER;
             float v[W];
@@ -1147,7 +1235,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                     for (int i = 0; i < W; ++i) acc[pb][pj * W + i] = __fadd_rn(acc[pb][pj * W + i], v[i]);
                 }
                 const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(tb * NMMA + b * BN + h * HALF + j * W);
-                mt_tmem_ld16(ta, v);
+                mt_tmem_ldw<W>(ta, v);
             }
             mt_tc_fence_before();
             __syncwarp();
@@ -1156,6 +1244,24 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
                 constexpr int lb = (NLD - 1) / PER, lj = (NLD - 1) % PER;
 #pragma unroll
                 for (int i = 0; i < W; ++i) acc[lb][lj * W + i] = __fadd_rn(acc[lb][lj * W + i], v[i]);
+            }
+        }
+        if constexpr (SACC) {
+            // the small products of the whole K, added once
+            if (ok && !mt_mbar_wait(sdone, 0, abort_flag, status, 5)) ok = false;
+            if (ok) {
+                __syncwarp();
+                mt_tc_fence_after();
+                constexpr int W = 16;
+                constexpr int PER = HALF / W;
+#pragma unroll
+                for (int l = 0; l < NB * PER; ++l) {
+                    const int b = l / PER, j = l % PER;
+                    float v[W];
+                    mt_tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(NACC * NMMA + b * BN + h * HALF + j * W), v);
+#pragma unroll
+                    for (int i = 0; i < W; ++i) acc[b][j * W + i] = __fadd_rn(acc[b][j * W + i], v[i]);
+                }
             }
         }
         if (ok) {

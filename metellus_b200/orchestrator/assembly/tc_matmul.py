@@ -40,6 +40,7 @@ from metellus_b200.orchestrator.assembly.expressions import (
     substitute,
     wrap_bool,
 )
+from metellus_b200.orchestrator.assembly import pipe_table
 from metellus_b200.orchestrator.assembly.extras import Extras, param_decl, pname
 from metellus_b200.orchestrator.ir import ElementwiseOp, MatmulOp, Scalar, Tensor
 from metellus_b200.orchestrator.kernel_group import STATUS_BYTES, STATUS_KEY, FusionStrategy, KernelGroup
@@ -127,9 +128,33 @@ def _pick_tile(M: int, N: int, nb: int, b_mn: bool = True, K: int = 0) -> tuple[
         bn, splitk = 128, 2
     else:
         bn = 64
+    return bn, _stages(bn, nb), splitk
+
+
+def _stages(bn: int, nb: int) -> int:
     tmem_stages = (512 - 2 * nb * bn) // 64
-    stages = max(2, min(4, tmem_stages, SMEM_BUDGET // (_raw_bytes(bn, nb) + _conv_bytes(bn, nb))))
-    return bn, stages, splitk
+    return max(2, min(4, tmem_stages, SMEM_BUDGET // (_raw_bytes(bn, nb) + _conv_bytes(bn, nb))))
+
+
+def _choose_tiling(M: int, N: int, K: int, nb: int, b_mn: bool) -> tuple[int, int, int, tuple | None]:
+    """(BN, stages, split-K, pair parameters or None) of a tcgen05 matmul group: the
+    measured pick of ``pipe_table`` where it covers the shape, else the heuristics
+    (``_pick_pair``, then ``_pick_tile``). Split-K exists for one anchor only."""
+    bn, stages, splitk = _pick_tile(M, N, nb, b_mn, K)
+    pair = _pick_pair(M, N, nb)
+    pick = pipe_table.lookup(M, N, K, nb)
+    if pick is not None and pick.variant == "pair":
+        pair = _pick_pair(M, N, nb, force=True)
+    elif pick is not None and pick.variant in ("one", "splitk"):
+        pair = None
+        if pick.variant == "splitk" and nb == 1 and -(-K // 32) >= 2:
+            bn, splitk = 128, 2
+        else:
+            splitk = 1
+        stages = _stages(bn, nb)
+    if pair is not None:
+        bn, splitk = pair[0], 1
+    return bn, stages, splitk, pair
 
 
 def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
@@ -139,24 +164,32 @@ def _smem_bytes(bn: int, stages: int, nb: int, b_mn: bool = True) -> int:
 # CTA-pair (cta_group::2) tiles: 256 x 128 per two-CTA cluster, 64 B rows per CTA.
 PAIR_RAW_BYTES = 128 * 32 * 4 + 64 * 32 * 4     # A + this CTA's half of B
 PAIR_CONV_BYTES = 2 * 64 * 32 * 4               # B hi + lo
-PAIR_NACC = 2     # accumulator buffers of 128 columns (3, with 2 converted stages, measured the same)
-PAIR_ISSUERS = 2    # MMA-issuing threads (warps 1 and 0: even / odd k-tiles); 1 measured 7-10 % slower
+# Accumulation (split accumulators): one issuing thread accumulates hi*hi into a chunk
+# buffer of 128 columns that the accumulator warps promote into fp32 registers every
+# PAIR_CHUNK k-tiles; a second thread accumulates the small products hi*lo + lo*hi of
+# the whole K into a buffer of their own, added once at the end.
+PAIR_SACC = int(os.environ.get("METELLUS_TC_SACC", "1"))
+PAIR_NACC = 1 if PAIR_SACC else 2   # chunk buffers of 128 columns
+PAIR_CHUNK = int(os.environ.get("METELLUS_TC_CHUNK", "3")) if PAIR_SACC else 1   # k-tiles per promotion
+PAIR_ISSUERS = 2    # MMA-issuing threads (warps 1 and 0); 1 measured 7-10 % slower
 PAIR_THREADS = 544  # 17 warps (both GEMM kernels): the 17th issues the TMA loads
-PAIR_CSTAGES = (512 - 128 * PAIR_NACC) // 64    # tensor memory: accumulators + 64 columns of A per stage
+# tensor memory: accumulator buffers + 64 columns of A (hi, lo) per converted stage
+PAIR_CSTAGES = (512 - 128 * (PAIR_NACC + PAIR_SACC)) // 64
 
 
 def pair_enabled() -> bool:
     return os.environ.get("METELLUS_TC_PAIR", "1") != "0"
 
 
-def _pick_pair(M: int, N: int, nb: int) -> tuple[int, int, int] | None:
+def _pick_pair(M: int, N: int, nb: int, force: bool = False) -> tuple[int, int, int] | None:
     """(BN, raw stages, converted stages) of a CTA-pair tile, or None when the output
-    has too few 256 x 128 pair tiles to fill the SMs (about one pair per two SMs)."""
+    has too few 256 x 128 pair tiles to fill the SMs (about one pair per two SMs)
+    and ``force`` is not set."""
     if not pair_enabled():
         return None
     bn = 128 // nb
     pairs = -(-M // 256) * -(-N // bn)
-    if pairs < 0.8 * SM_COUNT / 2:
+    if pairs < 0.8 * SM_COUNT / 2 and not force:
         return None
     cst = PAIR_CSTAGES
     rst = max(2, min(6, (SMEM_BUDGET - cst * PAIR_CONV_BYTES) // PAIR_RAW_BYTES))
@@ -164,7 +197,7 @@ def _pick_pair(M: int, N: int, nb: int) -> tuple[int, int, int] | None:
 
 
 def _pair_smem_bytes(rst: int, cst: int) -> int:
-    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 2) * 8 + 16 + 1024
+    return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 3) * 8 + 16 + 1024
 
 
 def _read(t: Tensor, mode: BroadcastSpec, row: str, col: str) -> str:
@@ -245,12 +278,10 @@ class TcGemmFragment:
         tb1 = "&tm_b1" if self.nb > 1 else "&tm_b0"
         if self.pair is not None:
             rst, cst = self.pair
-            # CHUNK 1: promote every 32-deep k-tile (2 measured ~6% faster but 4.9e-7
-            # normwise at 4096^3 against 3.2e-7, above an fp32 CPU product's 3.7e-7);
             # BAL: warps 2-3 split B while warps 4-7 split A (~1% faster)
             lines.append(
-                f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, 1, true, "
-                f"{PAIR_NACC}, {PAIR_ISSUERS}>"
+                f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, {PAIR_CHUNK}, "
+                f"true, {PAIR_NACC}, {PAIR_ISSUERS}, {str(bool(PAIR_SACC)).lower()}>"
                 f"(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);")
             return "\n".join(lines)
         lines.append(
@@ -300,8 +331,13 @@ def _fits_cap(nbytes: int) -> bool:
     return nbytes <= fusion.TGMEM_CAP_BYTES
 
 
-def _common_checks(a_src: Tensor, b_src: Tensor, M: int, N: int, K: int) -> tuple[str, str] | None:
-    if not tc_enabled() or M * N * K < MIN_VOLUME or not _fits_cap(SMEM_BUDGET):
+def _common_checks(a_src: Tensor, b_src: Tensor, M: int, N: int, K: int, nb: int = 1) -> tuple[str, str] | None:
+    if not tc_enabled() or not _fits_cap(SMEM_BUDGET):
+        return None
+    pick = pipe_table.lookup(M, N, K, nb)
+    if pick is not None and pick.variant == "ffma":
+        return None
+    if pick is None and M * N * K < MIN_VOLUME:
         return None
     la, lb = _a_layout(a_src), _b_layout(b_src)
     if la is None or lb is None:
@@ -343,10 +379,7 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
         for o in op.inputs:
             if o.name not in {e.out.name for e in decision.epilogue} and o.name != anchor.out.name:
                 extras.add_tensor(o, base)
-    bn, stages, splitk = _pick_tile(M, N, 1, lb == "mn", K)
-    pair = _pick_pair(M, N, 1)
-    if pair is not None:
-        bn, splitk = pair[0], 1
+    bn, stages, splitk, pair = _choose_tiling(M, N, K, 1, lb == "mn")
     need_col_check = N % 32 != 0
     epi = _epi_function(decision.epilogue, {anchor.out.name: "v[0][J]"}, out_key,
                         final_out.name, N, N, need_col_check)
@@ -383,7 +416,7 @@ def dual_gemm_eligible(a0: MatmulOp, a1: MatmulOp) -> bool:
         return False
     M, K = a0.a.shape
     N = a0.b.shape[1]
-    lay = _common_checks(a0.a, a0.b, M, N, K)
+    lay = _common_checks(a0.a, a0.b, M, N, K, 2)
     return lay is not None and _b_layout(a1.b) == lay[1]
 
 
@@ -402,7 +435,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
     N = a0.b.shape[1]
     if a1.a.shape[1] != K:
         return None
-    lay = _common_checks(a0.a, a0.b, M, N, K)
+    lay = _common_checks(a0.a, a0.b, M, N, K, 2)
     if lay is None or _b_layout(a1.b) != lay[1]:
         return None
     la, lb = lay
@@ -418,10 +451,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
         for o in op.inputs:
             if o.name not in inside:
                 extras.add_tensor(o, out_slot + 1)
-    bn, stages, _ = _pick_tile(M, N, 2, lb == "mn", K)
-    pair = _pick_pair(M, N, 2)
-    if pair is not None:
-        bn = pair[0]
+    bn, stages, _, pair = _choose_tiling(M, N, K, 2, lb == "mn")
     epi = _epi_function(tuple(epi_ops), {a0.out.name: "v[0][J]", a1.out.name: "v[1][J]"}, out_key,
                         merge.out.name, N, N, N % 32 != 0)
     bindings = (*in_keys, out_key, *extras.bindings)
