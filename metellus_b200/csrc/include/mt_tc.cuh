@@ -395,21 +395,22 @@ __host__ __device__ constexpr uint32_t mt_idesc_tf32(int M, int N, bool a_mn_maj
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// Veltkamp's splitting (T. J. Dekker, "A floating-point technique for extending the
-// available precision", Numer. Math. 18, 1971) with constant 2^13 + 1: hi carries the
-// leading 24 - 13 = 11 significant bits of x rounded to nearest, so it is exact as a
-// tf32, and lo = x - hi is exact with at most 12 significant bits (the MMA's truncating
-// read keeps 11 of them). Four fp32 operations on the FMA pipe and none on the integer
-// pipe (a bit-mask rounding spends ~7 integer ops per element, and the converter
-// warps were integer-pipe bound with it). Rounding hi to nearest rather than letting
-// the MMA truncate x halves |lo| and quarters the lo*lo term that 3xTF32 omits
-// (truncated hi measured 4.5e-7 normwise at 4096^3, nearest 3.2e-7; fp32 dot products
-// 3.7e-7). Where the product overflows (|x| > ~4e34, or x inf / NaN) hi falls back
-// to x with its low 13 mantissa bits cleared.
+// Split x into hi + lo with hi exact as a tf32 (x's leading 11 significant bits,
+// rounded to nearest on the magnitude, ties away from zero) and lo = x - hi, exact in
+// fp32 with at most 12 significant bits (the MMA's truncating read keeps 11 of them).
+// Rounding is done on the bit pattern: adding half a tf32 ulp (bit 12) to the
+// magnitude bits carries into the kept bits exactly when the dropped part is at least
+// half an ulp, then the 13 low bits are cleared. Two integer operations and one fp32
+// subtraction per element; this measured 6 % faster in the pair GEMM than Veltkamp's
+// splitting with an overflow guard (4 fp32 operations plus 3 for the guard), at
+// the same error. Rounding hi to nearest rather than letting the MMA truncate x halves
+// |lo| and quarters the lo*lo term that 3xTF32 omits (truncated hi measured 4.5e-7
+// normwise at 4096^3, nearest 3.2e-7; fp32 dot products 3.7e-7).
+// Range: exact for every finite |x| below (2 - 2^-11) * 2^127 (within half a tf32 ulp
+// of FLT_MAX the rounding carries to inf); inf stays inf and NaN stays NaN, and lo is
+// then NaN, so an inf or NaN operand makes the products it enters NaN.
 __device__ __forceinline__ void mt_split_tf32(float x, float& hi, float& lo) {
-    const float t = __fmul_rn(x, 8193.0f);
-    const float h = __fsub_rn(t, __fsub_rn(t, x));
-    hi = fabsf(t) <= 3.402823466e38f ? h : __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
     lo = __fsub_rn(x, hi);
 }
 
