@@ -511,7 +511,7 @@ def main() -> None:
         dom_bytes = kernel_bytes(gdom, ops)
         achieved = dom_bytes / (group_ms[j] / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": committed_traffic(key, gdom, world),
+                "frac": achieved / pk["hbm_gbs"], "traffic": None if overrides else committed_traffic(key, gdom, world),
                 "kernel": gdom.kernel.function_name, "peak_src": f"{pk['src']} hbm_gbs",
                 "algorithmic_bytes": dom_bytes}
     else:
@@ -519,7 +519,7 @@ def main() -> None:
         achieved = kflops / (group_ms[j] / 1e3) / 1e12
         pipe_peak, src = tensor_peak(gdom, pk)
         roof = {"bound": "tensor", "achieved": achieved, "peak": pipe_peak, "unit": "TFLOP/s",
-                "frac": achieved / pipe_peak, "traffic": committed_traffic(key, gdom, world),
+                "frac": achieved / pipe_peak, "traffic": None if overrides else committed_traffic(key, gdom, world),
                 "kernel": gdom.kernel.function_name, "peak_src": src, "algorithmic_flops": kflops}
 
     # the same full configuration on every rank (weak scaling), for comparison

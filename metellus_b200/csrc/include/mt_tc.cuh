@@ -892,6 +892,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 #endif
 
 // ---------------------------------------------------------------------------------
+
 // Columns per tensor-memory load when the accumulator warps drain a chunk buffer.
 #ifndef MT_PAIR_DRAIN_W
 #define MT_PAIR_DRAIN_W 16
@@ -926,7 +927,7 @@ __device__ __forceinline__ void mt_gemm_3xtf32(const mt_tmap* tmA, const mt_tmap
 // (multicast commit). Every wait is bounded; both CTAs meet at a cluster barrier
 // before tensor memory is freed and either exits.
 template <int BN, int RST, int CST, bool B_MN, int NB, int CHUNK, bool BAL, int NACC, int NISSUE, bool SACC,
-          class ProA, class ProB, class Epi>
+          int GROUP_M, class ProA, class ProB, class Epi>
 __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt_tmap* tmB0, const mt_tmap* tmB1,
                                                     int M, int N, int K, const ProA& proA, const ProB& proB,
                                                     const Epi& epi, int* status, void* smem_raw) {
@@ -967,7 +968,9 @@ __device__ __forceinline__ void mt_gemm_3xtf32_pair(const mt_tmap* tmA, const mt
     MT_PROF_DECL();
     int m0, n0;
     {
-        constexpr int kGroupM = 8;              // in 256-row pair tiles
+        // consecutive clusters walk the N tiles of a group of GROUP_M M tiles, so the
+        // ~74 clusters resident at once share A and B tiles in L2
+        constexpr int kGroupM = GROUP_M;        // in 256-row pair tiles
         const int n_tiles = (int)gridDim.x / 2, m_tiles = (int)gridDim.y;
         const int id = (int)(blockIdx.y * n_tiles + blockIdx.x / 2);
         const int group = id / (kGroupM * n_tiles);

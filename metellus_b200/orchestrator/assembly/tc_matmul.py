@@ -196,6 +196,18 @@ def _pick_pair(M: int, N: int, nb: int, force: bool = False) -> tuple[int, int, 
     return bn, rst, cst
 
 
+def _pair_group_m(K: int) -> int:
+    """M tiles (of 256 rows) per group of the pair kernel's tile order. Consecutive
+    clusters walk all N tiles of one group, so each group's A rows stay in L2 while
+    the whole B panel streams past, and B is read once per group. Measured on the C5
+    GEMMs (DRAM bytes per launch, ncu): the dual GEMM (K = 2048, 2 MB of A per M
+    tile) reads 4.36 / 2.27 / 1.21 / 0.68 / 2.48 GB with groups of 2 / 4 / 8 / 16 / 32
+    (32 overflows L2); the down-projection (K = 8192, 8 MB per M tile) 1.81 / 2.01 /
+    2.09 / 2.73 / 5.76 GB. So about 32 MB of A per group, and at least 2 tiles."""
+    a_tile = 256 * K * 4
+    return 16 if (32 << 20) // a_tile >= 16 else 2
+
+
 def _pair_smem_bytes(rst: int, cst: int) -> int:
     return rst * PAIR_RAW_BYTES + cst * PAIR_CONV_BYTES + (2 * rst + 2 * cst + 2 * PAIR_NACC + 3) * 8 + 16 + 1024
 
@@ -251,6 +263,7 @@ class TcGemmFragment:
     epi_body: str               # body of the per-(row, 32 columns) store lambda
     splitk: int = 1             # 2: two-CTA cluster per tile, K halves combined via DSMEM
     pair: tuple[int, int] | None = None  # (raw, converted) stages of a CTA-pair tile
+    group_m: int = 8            # pair tiles: M tiles per group of the tile order
     name: str = "tc_gemm"
     kind: str = "compute"
 
@@ -281,7 +294,7 @@ class TcGemmFragment:
             # BAL: warps 2-3 split B while warps 4-7 split A (~1% faster)
             lines.append(
                 f"mt_gemm_3xtf32_pair<{self.bn}, {rst}, {cst}, {str(self.b_mn).lower()}, {self.nb}, {PAIR_CHUNK}, "
-                f"true, {PAIR_NACC}, {PAIR_ISSUERS}, {str(bool(PAIR_SACC)).lower()}>"
+                f"true, {PAIR_NACC}, {PAIR_ISSUERS}, {str(bool(PAIR_SACC)).lower()}, {self.group_m}>"
                 f"(&tm_a, &tm_b0, {tb1}, (int)M, (int)N, (int)K, pro_a, pro_b, epi, g_status, tc_arena);")
             return "\n".join(lines)
         lines.append(
@@ -390,7 +403,8 @@ def try_assemble_tc_matmul(decision: DecisionView, function_name: str | None) ->
         _tmap(bindings.index(src_b.buffer_key), src_b, lb, 64 if pair else bn),
     )
     frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=1, pro_a=pro_a,
-                          pro_b=pro_b, epi_body=epi, splitk=splitk, pair=pair[1:] if pair else None)
+                          pro_b=pro_b, epi_body=epi, splitk=splitk, pair=pair[1:] if pair else None,
+                          group_m=_pair_group_m(K))
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_matmul_{anchor.out.name}_fused"
     ctx = CodegenContext(
@@ -462,7 +476,7 @@ def try_assemble_tc_multi_anchor(decision: DecisionView, function_name: str | No
         _tmap(bindings.index(a1.b.buffer_key), a1.b, lb, 64 if pair else bn),
     )
     frag = TcGemmFragment(bn=bn, stages=stages, a_mn=la == "mn", b_mn=lb == "mn", nb=2, pro_a=None, pro_b=None,
-                          epi_body=epi, pair=pair[1:] if pair else None)
+                          epi_body=epi, pair=pair[1:] if pair else None, group_m=_pair_group_m(K))
     n_arena = frag.arena_bytes // 4
     fn = function_name or f"tc_diamond_{merge.out.name}_fused"
     ctx = CodegenContext(
