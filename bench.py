@@ -483,11 +483,21 @@ def main() -> None:
     # region and the timed region itself (nvidia-smi samples every 100 ms).
     sampler = ClockSampler(local)
     sampler.start()
-    t_soak = time.perf_counter()
-    while not args.profile and time.perf_counter() - t_soak < 1.0:
+    # The soak runs the same number of steps on every rank: a step of a combined
+    # reduction holds an NCCL all-reduce, and ranks that each looped "for 1 s" ran
+    # different numbers of them and hung. One batch of 8 steps is timed per rank and
+    # the largest batch count any rank needs for ~1 s is used everywhere.
+    if not args.profile:
+        t0 = time.perf_counter()
         for _ in range(8):
             prep.timed_step()
         backend.sync()
+        batches = max(0, math.ceil(1.0 / max(time.perf_counter() - t0, 1e-6)) - 1)
+        batches = int(max_over_ranks(float(batches)))
+        for _ in range(batches):
+            for _ in range(8):
+                prep.timed_step()
+            backend.sync()
     barrier()
     t_wall = time.perf_counter()
     step_ms = prep.time_steps(args.steps)
